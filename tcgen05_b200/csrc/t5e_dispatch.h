@@ -1,0 +1,21 @@
+// t5e_dispatch.h -- internal interface between the C ABI layer and the
+// specialised kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "t5e.h"
+
+namespace t5e {
+
+// Launches a specialised kernel when one covers (model, batch); returns
+// T5E_ERR_UNSUPPORTED (and launches nothing) otherwise.
+int launch_fast(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
+
+// Records the last launch error for t5e_last_error(); T5E_OK or T5E_ERR_CUDA.
+int kernel_status(const char* what);
+
+// Grid size for a grid-stride loop over n items.
+int grid_for(uint64_t n, int block);
+
+}  // namespace t5e

@@ -1,0 +1,622 @@
+"""Scalar, matrix and batched entry points of the tcgen05 MMA emulator.
+
+``mma_dot`` and ``mma`` keep the signatures and ValueError behaviour of the
+reference's tcgen05_model/simulator.py:80-211; ``mma_dot_batch`` and
+``mma_batch`` evaluate N independent dot products or T independent tiles in
+one kernel launch.  All arithmetic runs in the CUDA library; the host only
+validates arguments, packs operand rows and moves buffers.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import numpy as np
+
+from . import _native as nat
+from . import packing
+from . import runtime
+from .model import DotProduct, ScalarModel, _ModelBase, make_model, normalize_format
+
+SPARSE_TF32_SELECTORS = frozenset((0x4, 0xE))
+SPARSE_2OF4_SELECTORS = frozenset((0x4, 0x8, 0xC, 0x9, 0xD, 0x6, 0xE))
+
+
+def _matrix(value: Sequence[Sequence[int]], name: str) -> tuple[tuple[int, ...], ...]:
+    """Row-major matrix checks of tcgen05_model/simulator.py:13-23."""
+    rows = tuple(tuple(row) for row in value)
+    if not rows or not rows[0]:
+        raise ValueError(f"{name} must be a non-empty matrix")
+    width = len(rows[0])
+    if any(len(row) != width for row in rows):
+        raise ValueError(f"{name} must be rectangular")
+    for word in (word for row in rows for word in row):
+        if not isinstance(word, (int, np.integer)) or isinstance(word, bool) or not 0 <= word <= 0xFFFF_FFFF:
+            raise ValueError(f"{name} contains a non-uint32 word: {word!r}")
+    return rows
+
+
+def _sparse_geometry(format_name: str, kind: str | None, nvfp4: bool = False) -> tuple[int, int]:
+    """(T5E_SPARSE_* mode, chunk size) of a descriptor; validates ``kind``."""
+    if kind not in (None, "mxf8f6f4", "mxf4", "mxf4nvf4", "nvfp4"):
+        raise ValueError(f"unsupported sparse metadata kind: {kind!r}")
+    if format_name == "tf32":
+        return nat.SPARSE_1OF2, 2
+    if nvfp4 or kind in ("mxf4", "mxf4nvf4", "nvfp4"):
+        return nat.SPARSE_4OF8, 8
+    return nat.SPARSE_2OF4, 4
+
+
+def sparse_active_indices(
+    format_name: str,
+    k: int,
+    metadata: int | Sequence[int],
+    *,
+    kind: str | None = None,
+    nvfp4: bool = False,
+) -> frozenset[int]:
+    """Logical K indices selected by tcgen05 sparse metadata
+    (tcgen05_model/simulator.py:26-77).
+
+    TF32 keeps one value of each pair (selector 0x4: lower, 0xE: upper);
+    BF16/F16/f8/f6/f4 keep two of each four (the selector's low and high
+    2-bit fields); kind "mxf4", "mxf4nvf4" or "nvfp4" keeps two adjacent
+    pairs of each eight.  Nibbles are read least significant first; an int
+    metadata word repeats over K.
+    """
+    format_name = normalize_format(format_name)
+    kind = None if kind is None else kind.lower()
+    mode, chunk_size = _sparse_geometry(format_name, kind, nvfp4)
+    words = (metadata,) if isinstance(metadata, (int, np.integer)) else tuple(metadata)
+    if not words or any(not 0 <= word <= 0xFFFF_FFFF for word in words):
+        raise ValueError("metadata must contain uint32 words")
+    chunks = (k + chunk_size - 1) // chunk_size
+    if isinstance(metadata, (int, np.integer)):
+        words = words * ((chunks + 7) // 8)
+    if len(words) * 8 < chunks:
+        raise ValueError(f"{chunks} metadata nibbles are required for K={k}")
+    legal = SPARSE_TF32_SELECTORS if mode == nat.SPARSE_1OF2 else SPARSE_2OF4_SELECTORS
+    active: set[int] = set()
+    for chunk in range(chunks):
+        selector = (int(words[chunk // 8]) >> ((chunk & 7) * 4)) & 0xF
+        if selector not in legal:
+            raise ValueError(f"illegal sparse selector 0x{selector:x} in chunk {chunk}")
+        if mode == nat.SPARSE_1OF2:
+            active.add(chunk * 2 + (selector == 0xE))
+            continue
+        low, high = selector & 3, (selector >> 2) & 3
+        if mode == nat.SPARSE_4OF8:
+            for pair in (low, high):
+                active.update((chunk * 8 + pair * 2, chunk * 8 + pair * 2 + 1))
+        else:
+            active.update((chunk * 4 + low, chunk * 4 + high))
+    return frozenset(index for index in active if index < k)
+
+
+# ---------------------------------------------------------------- helpers
+
+
+def _is_torch(x) -> bool:
+    try:
+        import torch
+    except ImportError:  # pragma: no cover - torch is a dependency
+        return False
+    return isinstance(x, torch.Tensor)
+
+
+def _words_np(x, name: str) -> np.ndarray:
+    """Host array of raw words checked to be uint32 values (as int64)."""
+    arr = np.asarray(x)
+    if arr.dtype == object or arr.dtype.kind not in "iu":
+        try:
+            arr = np.asarray(x, dtype=np.int64)
+        except (OverflowError, TypeError, ValueError) as exc:
+            raise ValueError(f"{name} contains a non-uint32 word") from exc
+    if arr.dtype.kind == "u" and arr.dtype.itemsize <= 4:
+        return arr.astype(np.uint32)
+    if arr.size and (arr.min() < 0 or arr.max() > 0xFFFF_FFFF):
+        bad = arr[(arr < 0) | (arr > 0xFFFF_FFFF)].flat[0]
+        raise ValueError(f"operand is not a uint32 word: {int(bad)!r}")
+    return arr.astype(np.uint32)
+
+
+def _scales_np(x, name: str) -> np.ndarray:
+    arr = np.asarray(x)
+    if arr.dtype == object or arr.dtype.kind not in "iu":
+        arr = np.asarray(x, dtype=np.int64)
+    if arr.size and (arr.min() < 0 or arr.max() > 0xFF):
+        bad = arr[(arr < 0) | (arr > 0xFF)].flat[0]
+        raise ValueError(f"scale is not an 8-bit word: {int(bad)!r}")
+    return arr.astype(np.uint8)
+
+
+def _c_dtype_bytes(model) -> int:
+    return 2 if model.descriptor().d_type == nat.D_F16 else 4
+
+
+def _c_words_on_device(c_dev, f16: bool):
+    """C words already on the device -> the dtype the kernel reads."""
+    import torch
+
+    want = 2 if f16 else 4
+    if c_dev.element_size() == want and c_dev.dtype in (torch.int16, torch.uint16, torch.int32, torch.uint32):
+        return c_dev.view(torch.int16 if f16 else torch.int32).contiguous()
+    wide = c_dev.to(torch.int64)
+    if f16:
+        return wide.bitwise_and(0xFFFF).to(torch.int32).to(torch.int16).contiguous()
+    return wide.bitwise_and(0xFFFFFFFF).to(torch.int32).contiguous()
+
+
+def _c_host(c, n: int, model) -> np.ndarray:
+    """C words as the dtype the kernel reads (uint16 for F16 C, else uint32)."""
+    words = np.zeros(n, dtype=np.uint32) if c is None else _words_np(c, "C").reshape(n)
+    if _c_dtype_bytes(model) == 2:
+        return (words & 0xFFFF).astype(np.uint16)
+    return words
+
+
+def _check_scale_pair(model, k_phys: int, nsa: int | None, nsb: int | None) -> int:
+    """Scale-count rules of the scaled models (model.py:725-731, :852-858);
+    returns the per-operand scale count the kernel reads (0: defaults)."""
+    if (nsa is None) != (nsb is None):
+        raise ValueError("scale_a and scale_b must be supplied together")
+    d = model.descriptor()
+    if d.family not in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED):
+        return -1  # scales are ignored by this family
+    if nsa is None:
+        return 0
+    if nsa != nsb:
+        raise ValueError(model._scale_count_error)
+    if nsa * d.scale_block < k_phys:
+        raise ValueError(model._scale_cover_error)
+    return nsa
+
+
+def _eval_case_arrays(model, a, b, c, sa, sb, *, device=None) -> np.ndarray:
+    """Evaluate dense cases given as host word arrays (used by model.eval)."""
+    a = _words_np(a, "A")
+    b = _words_np(b, "B")
+    n, k = a.shape
+    if b.shape != (n, k):
+        raise ValueError("A and B dot-product vectors must have equal length")
+    if k == 0:
+        raise ValueError("a dot product must contain at least one element")
+    if k > nat.MAX_K:
+        raise ValueError(f"K={k} exceeds the emulator's maximum of {nat.MAX_K}")
+    if sa is not None:
+        sa = _scales_np(sa, "scale_a").reshape(n, -1)
+    if sb is not None:
+        sb = _scales_np(sb, "scale_b").reshape(n, -1)
+    nscale = _check_scale_pair(model, k, None if sa is None else sa.shape[1], None if sb is None else sb.shape[1])
+    desc = model.descriptor()
+    dev = runtime.require_device(device)
+    batch = runtime.DeviceBatch(
+        n=n,
+        k=k,
+        a=runtime.to_device(packing.pack_rows(a, desc.a_format), dev),
+        b=runtime.to_device(packing.pack_rows(b, desc.b_format), dev),
+        c=runtime.to_device(_c_host(c, n, model), dev),
+    )
+    if nscale > 0:
+        batch.scale_a = runtime.to_device(sa, dev)
+        batch.scale_b = runtime.to_device(sb, dev)
+    d, st = runtime.launch(desc, batch)
+    st_h = st.cpu().numpy()
+    if st_h.any():
+        first = int(np.flatnonzero(st_h)[0])
+        _raise_case_status(model, int(st_h[first]))
+    return d.cpu().numpy().view(np.uint32).copy()
+
+
+def _raise_case_status(model, status: int, *, meta_message=None) -> None:
+    if status == nat.CASE_EMPTY:
+        raise ValueError("a dot product must contain at least one element")
+    if status == nat.CASE_SCALE_COVER:
+        raise ValueError(model._scale_cover_error)
+    if status in (nat.CASE_BAD_SELECTOR, nat.CASE_META_WORDS) and meta_message is not None:
+        meta_message()
+    raise ValueError(f"invalid case (status {status})")
+
+
+# ------------------------------------------------------------ scalar API
+
+
+def mma_dot(
+    a: Sequence[int],
+    b: Sequence[int],
+    c: int = 0,
+    *,
+    model: ScalarModel | None = None,
+    a_format: str = "tf32",
+    b_format: str | None = None,
+    d_type: str = "f32",
+    saturate: bool = False,
+    scaling: str | None = None,
+    scale_vec: int | None = None,
+    kind: str | None = None,
+    scale_a: Sequence[int] | None = None,
+    scale_b: Sequence[int] | None = None,
+    sparse_metadata: int | Sequence[int] | None = None,
+) -> int:
+    """One tcgen05 output word (tcgen05_model/simulator.py:80-140), evaluated
+    on the GPU.  Sparse calls take full logical-K A/B; disabled positions are
+    dropped before classification (masked for unscaled formats, compressed
+    to physical K before scale-block assignment for scaled ones)."""
+    a_words, b_words = tuple(a), tuple(b)
+    if len(a_words) != len(b_words):
+        raise ValueError("A and B dot-product vectors must have equal length")
+    if sparse_metadata is not None:
+        active = sparse_active_indices(
+            a_format,
+            len(a_words),
+            sparse_metadata,
+            kind="nvfp4" if (scaling or "").lower() == "ue4m3" else kind,
+        )
+        if scaling is None:
+            a_words = tuple(word if index in active else 0 for index, word in enumerate(a_words))
+            b_words = tuple(word if index in active else 0 for index, word in enumerate(b_words))
+        else:
+            order = sorted(active)
+            a_words = tuple(a_words[index] for index in order)
+            b_words = tuple(b_words[index] for index in order)
+    selected = model or make_model(
+        a_format,
+        b_format,
+        d_type=d_type,
+        saturate=saturate,
+        scaling=scaling,
+        scale_vec=scale_vec,
+        sparse=False if scaling is not None else sparse_metadata is not None,
+        kind=kind,
+    )
+    case = DotProduct(
+        a_words,
+        b_words,
+        c,
+        None if scale_a is None else tuple(scale_a),
+        None if scale_b is None else tuple(scale_b),
+    )
+    return selected.eval(case)
+
+
+def mma(
+    a: Sequence[Sequence[int]],
+    b: Sequence[Sequence[int]],
+    c: Sequence[Sequence[int]] | None = None,
+    *,
+    a_format: str = "tf32",
+    b_format: str | None = None,
+    d_type: str = "f32",
+    saturate: bool = False,
+    scaling: str | None = None,
+    scale_vec: int | None = None,
+    kind: str | None = None,
+    scale_a: Sequence[Sequence[int]] | None = None,
+    scale_b: Sequence[Sequence[int]] | None = None,
+    sparse_metadata: int | Sequence[int] | None = None,
+) -> tuple[tuple[int, ...], ...]:
+    """``D = A @ B + C`` on row-major raw-word matrices
+    (tcgen05_model/simulator.py:143-211): every output word is the scalar
+    model of one row of A and one column of B, all evaluated in one launch.
+    ``scale_a`` is indexed by A row, ``scale_b`` by B column."""
+    a_rows, b_rows = _matrix(a, "A"), _matrix(b, "B")
+    m, k, n = len(a_rows), len(a_rows[0]), len(b_rows[0])
+    if len(b_rows) != k:
+        raise ValueError(f"A is {m}x{k} but B has {len(b_rows)} rows")
+    c_rows = tuple((0,) * n for _ in range(m)) if c is None else _matrix(c, "C")
+    if len(c_rows) != m or len(c_rows[0]) != n:
+        raise ValueError(f"C must be {m}x{n}")
+    sa_rows = None if scale_a is None else _matrix(scale_a, "scale_a")
+    sb_rows = None if scale_b is None else _matrix(scale_b, "scale_b")
+    if (sa_rows is None) != (sb_rows is None):
+        raise ValueError("scale_a and scale_b must be supplied together")
+    if sa_rows is not None and (len(sa_rows) != m or len(sb_rows) != n):
+        raise ValueError("scale_a needs one row per A row and scale_b one row per B column")
+    model = make_model(
+        a_format,
+        b_format,
+        d_type=d_type,
+        saturate=saturate,
+        scaling=scaling,
+        scale_vec=scale_vec,
+        sparse=sparse_metadata is not None,
+        kind=kind,
+    )
+    result = mma_batch(
+        np.array(a_rows, dtype=np.int64)[None],
+        np.array(b_rows, dtype=np.int64)[None],
+        np.array(c_rows, dtype=np.int64)[None],
+        model=model,
+        a_format=a_format,
+        scaling=scaling,
+        kind=kind,
+        scale_a=None if sa_rows is None else np.array(sa_rows, dtype=np.int64)[None],
+        scale_b=None if sb_rows is None else np.array(sb_rows, dtype=np.int64)[None],
+        sparse_metadata=sparse_metadata,
+    )
+    return tuple(tuple(int(w) for w in row) for row in result[0])
+
+
+# ----------------------------------------------------------- batched API
+
+
+class PackedRows:
+    """Operand rows already in the kernels' packed layout (see packing.py):
+    ``data`` is a [rows, stride] uint8 array or tensor, ``k`` the elements per
+    row (the selected count for a compressed sparse A)."""
+
+    def __init__(self, data, k: int, compressed: bool = False):
+        self.data = data
+        self.k = k
+        self.compressed = compressed
+
+
+def _metadata_array(sparse_metadata, rows: int):
+    """Metadata as ([R or 1, W] uint32 host/tensor, flags)."""
+    if isinstance(sparse_metadata, (int, np.integer)):
+        if not 0 <= sparse_metadata <= 0xFFFF_FFFF:
+            raise ValueError("metadata must contain uint32 words")
+        return np.array([[sparse_metadata]], dtype=np.uint32), nat.FLAG_META_REPEAT | nat.FLAG_META_BROADCAST
+    if isinstance(sparse_metadata, (list, tuple)):
+        words = tuple(sparse_metadata)
+        if not words or any(not 0 <= int(w) <= 0xFFFF_FFFF for w in words):
+            raise ValueError("metadata must contain uint32 words")
+        return np.array([words], dtype=np.uint32), nat.FLAG_META_BROADCAST
+    if _is_torch(sparse_metadata):
+        t = sparse_metadata
+        if t.dim() == 1:
+            return t.reshape(-1, 1), nat.FLAG_META_REPEAT
+        return t, 0
+    arr = _words_np(sparse_metadata, "metadata")
+    if arr.ndim == 1:
+        return arr.reshape(-1, 1), nat.FLAG_META_REPEAT
+    return arr, 0
+
+
+def _operand_rows(x, fmt: int, dev, name: str):
+    """Host/device words or PackedRows -> (device uint8 [R, stride], rows, k)."""
+    import torch
+
+    if isinstance(x, PackedRows):
+        return runtime.to_device(x.data, dev, torch.uint8), x.data.shape[0], x.k
+    if _is_torch(x) and x.is_cuda:
+        if x.dim() != 2:
+            raise ValueError(f"{name} must be a [N, K] array of words")
+        return packing.pack_rows_device(x.to(dev), fmt), x.shape[0], x.shape[1]
+    words = _words_np(x, name)
+    if words.ndim != 2:
+        raise ValueError(f"{name} must be a [N, K] array of words")
+    return runtime.to_device(packing.pack_rows(words, fmt), dev), words.shape[0], words.shape[1]
+
+
+def _prepare(model, a_format, scaling, kind, k, rows_a, sparse_metadata):
+    if sparse_metadata is None:
+        return 0, None, 0
+    fmt = normalize_format(a_format)
+    meta_kind = "nvfp4" if (scaling or "").lower() == "ue4m3" else (None if kind is None else kind.lower())
+    mode, chunk = _sparse_geometry(fmt, meta_kind)
+    meta, flags = _metadata_array(sparse_metadata, rows_a)
+    chunks = (k + chunk - 1) // chunk
+    if not (flags & nat.FLAG_META_REPEAT) and meta.shape[1] * 8 < chunks:
+        raise ValueError(f"{chunks} metadata nibbles are required for K={k}")
+    return mode, meta, flags
+
+
+def _run(model, a_rows, b_rows, c_dev, k, dev, *, n, tile_m, tile_n, scale_a, scale_b, sparse, meta, flags,
+         a_compressed, check, meta_error, generic=False):
+    import torch
+
+    desc = model.descriptor()
+    batch = runtime.DeviceBatch(n=n, k=k, a=a_rows, b=b_rows, c=c_dev, tile_m=tile_m, tile_n=tile_n,
+                                sparse=sparse, flags=flags | (nat.FLAG_SPARSE_A_COMPRESSED if a_compressed else 0))
+    if scale_a is not None:
+        batch.scale_a = runtime.to_device(scale_a, dev, torch.uint8)
+        batch.scale_b = runtime.to_device(scale_b, dev, torch.uint8)
+    if meta is not None:
+        batch.metadata = runtime.to_device(meta, dev, torch.int32 if not _is_torch(meta) else None)
+    d, st = runtime.launch(desc, batch, status=check, generic=generic)
+    if check:
+        st_h = st.cpu().numpy()
+        if st_h.any():
+            first = int(np.flatnonzero(st_h)[0])
+            _raise_case_status(model, int(st_h[first]), meta_message=lambda: meta_error(first))
+    return d
+
+
+def mma_dot_batch(
+    a,
+    b,
+    c=None,
+    *,
+    model: ScalarModel | None = None,
+    a_format: str = "tf32",
+    b_format: str | None = None,
+    d_type: str = "f32",
+    saturate: bool = False,
+    scaling: str | None = None,
+    scale_vec: int | None = None,
+    kind: str | None = None,
+    scale_a=None,
+    scale_b=None,
+    sparse_metadata=None,
+    device=None,
+    check: bool = True,
+    generic: bool = False,
+    out=None,
+):
+    """N independent ``mma_dot`` evaluations in one kernel launch.
+
+    ``a``, ``b``: [N, K] raw container words (numpy arrays or torch tensors,
+    host or CUDA) or ``PackedRows``; sparse calls pass full logical-K rows
+    (or a compressed ``PackedRows`` A).  ``c``: [N] words or None (zeros).
+    ``scale_a``/``scale_b``: [N, blocks] 8-bit scales or None (the reference
+    defaults).  ``sparse_metadata``: an int (repeated over K) or a word
+    sequence shared by every case, or an array of N ints / [N, W] words.
+    Returns the N result words: a uint32 numpy array for host inputs, a
+    torch.uint32 CUDA tensor for device inputs, or ``out`` (a host array or
+    pinned tensor of N 32-bit words) filled in place.  With ``check`` the
+    per-case ValueErrors of the reference are raised.
+    """
+    import torch
+
+    selected = model or make_model(a_format, b_format, d_type=d_type, saturate=saturate, scaling=scaling,
+                                   scale_vec=scale_vec, kind=kind)
+    if not isinstance(selected, _ModelBase):
+        raise TypeError("model must come from tcgen05_b200.make_model or its model classes")
+    desc = selected.descriptor()
+    dev = runtime.require_device(device)
+    host_result = not ((_is_torch(a) and a.is_cuda) or (isinstance(a, PackedRows) and _is_torch(a.data)
+                                                        and a.data.is_cuda))
+    a_rows, n, ka = _operand_rows(a, desc.a_format, dev, "A")
+    b_rows, nb, k = _operand_rows(b, desc.b_format, dev, "B")
+    a_compressed = isinstance(a, PackedRows) and a.compressed
+    if nb != n:
+        raise ValueError("A and B must hold the same number of cases")
+    if ka != k and not a_compressed:
+        raise ValueError("A and B dot-product vectors must have equal length")
+    if k < 1:
+        raise ValueError("a dot product must contain at least one element")
+    if k > nat.MAX_K:
+        raise ValueError(f"K={k} exceeds the emulator's maximum of {nat.MAX_K}")
+    sparse, meta, flags = _prepare(selected, a_format, scaling, kind, k, n, sparse_metadata)
+    if c is None:
+        c_dev = torch.zeros(n, dtype=torch.int16 if desc.d_type == nat.D_F16 else torch.int32, device=dev)
+    elif _is_torch(c):
+        c_dev = _c_words_on_device(c.reshape(n).to(dev, non_blocking=True), desc.d_type == nat.D_F16)
+    else:
+        c_host = _c_host(c, n, selected)
+        c_dev = runtime.to_device(c_host.view(np.int16) if c_host.dtype == np.uint16 else c_host, dev)
+    if (scale_a is None) != (scale_b is None):
+        raise ValueError("scale_a and scale_b must be supplied together")
+    sa = sb = None
+    if scale_a is not None and desc.family in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED):
+        sa = scale_a if _is_torch(scale_a) else _scales_np(scale_a, "scale_a")
+        sb = scale_b if _is_torch(scale_b) else _scales_np(scale_b, "scale_b")
+        if sa.ndim == 1:
+            sa = sa.reshape(1, -1).repeat(n, 0) if not _is_torch(sa) else sa.reshape(1, -1).expand(n, -1)
+        if sb.ndim == 1:
+            sb = sb.reshape(1, -1).repeat(n, 0) if not _is_torch(sb) else sb.reshape(1, -1).expand(n, -1)
+        if sa.shape[1] != sb.shape[1]:
+            raise ValueError(selected._scale_count_error)
+        if sparse == 0 and sa.shape[1] * desc.scale_block < k:
+            raise ValueError(selected._scale_cover_error)
+
+    def meta_error(first: int) -> None:
+        record = meta[0] if meta.shape[0] == 1 else meta[first]
+        words = np.asarray(record.cpu() if _is_torch(record) else record).astype(np.int64).tolist()
+        sparse_active_indices(a_format, k, words[0] if flags & nat.FLAG_META_REPEAT else words,
+                              kind="nvfp4" if (scaling or "").lower() == "ue4m3" else kind)
+
+    d = _run(selected, a_rows, b_rows, c_dev, k, dev, n=n, tile_m=1, tile_n=1, scale_a=sa, scale_b=sb,
+             sparse=sparse, meta=meta, flags=flags, a_compressed=a_compressed, check=check, meta_error=meta_error,
+             generic=generic)
+    if out is not None:
+        if _is_torch(out):
+            out.copy_(d.view(out.dtype) if out.element_size() == 4 else d, non_blocking=True)
+            torch.cuda.current_stream(dev).synchronize()
+        else:
+            out[...] = d.cpu().numpy().view(np.uint32)
+        return out
+    if host_result:
+        return d.cpu().numpy().view(np.uint32).copy()
+    return d.view(torch.uint32)
+
+
+def mma_batch(
+    a,
+    b,
+    c=None,
+    *,
+    model: ScalarModel | None = None,
+    a_format: str = "tf32",
+    b_format: str | None = None,
+    d_type: str = "f32",
+    saturate: bool = False,
+    scaling: str | None = None,
+    scale_vec: int | None = None,
+    kind: str | None = None,
+    scale_a=None,
+    scale_b=None,
+    sparse_metadata=None,
+    device=None,
+    check: bool = True,
+    generic: bool = False,
+):
+    """T independent row-major tiles ``D[t] = A[t] @ B[t] + C[t]`` in one
+    launch: ``a`` [T, M, K], ``b`` [T, K, N], ``c`` [T, M, N] raw words;
+    ``scale_a`` [T, M, blocks], ``scale_b`` [T, N, blocks]; one metadata
+    value shared by all tiles (as ``mma``), or an array of T ints / [T, W]
+    words.  Returns [T, M, N] words (numpy for host inputs, torch.uint32 on
+    the device for device inputs)."""
+    import torch
+
+    selected = model or make_model(a_format, b_format, d_type=d_type, saturate=saturate, scaling=scaling,
+                                   scale_vec=scale_vec, kind=kind)
+    desc = selected.descriptor()
+    dev = runtime.require_device(device)
+    on_device = _is_torch(a) and a.is_cuda
+    if on_device:
+        t, m, k = a.shape
+        n = b.shape[2]
+        a_rows = packing.pack_rows_device(a.reshape(t * m, k).to(dev), desc.a_format)
+        b_rows = packing.pack_rows_device(b.to(dev).transpose(1, 2).reshape(t * n, k), desc.b_format)
+    else:
+        aw = _words_np(a, "A")
+        bw = _words_np(b, "B")
+        t, m, k = aw.shape
+        n = bw.shape[2]
+        if bw.shape[:2] != (t, k):
+            raise ValueError(f"A is {m}x{k} but B has {bw.shape[1]} rows")
+        a_rows = runtime.to_device(packing.pack_rows(aw.reshape(t * m, k), desc.a_format), dev)
+        b_rows = runtime.to_device(
+            packing.pack_rows(np.ascontiguousarray(bw.transpose(0, 2, 1)).reshape(t * n, k), desc.b_format), dev)
+    if k > nat.MAX_K:
+        raise ValueError(f"K={k} exceeds the emulator's maximum of {nat.MAX_K}")
+    total = t * m * n
+    if c is None:
+        c_dev = torch.zeros(total, dtype=torch.int16 if desc.d_type == nat.D_F16 else torch.int32, device=dev)
+    elif _is_torch(c) and c.is_cuda:
+        c_dev = c.reshape(total).to(dev)
+        want = 2 if desc.d_type == nat.D_F16 else 4
+        if c_dev.element_size() != want:
+            c_dev = c_dev.to(torch.int64).bitwise_and(0xFFFF if want == 2 else 0xFFFFFFFF)
+            c_dev = c_dev.to(torch.int32).to(torch.int16) if want == 2 else c_dev.to(torch.int32)
+    else:
+        c_host = _c_host(np.asarray(c).reshape(total), total, selected)
+        c_dev = runtime.to_device(c_host.view(np.int16) if c_host.dtype == np.uint16 else c_host, dev)
+    sa = sb = None
+    if (scale_a is None) != (scale_b is None):
+        raise ValueError("scale_a and scale_b must be supplied together")
+    if scale_a is not None and desc.family in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED):
+        sa = scale_a.reshape(t * m, -1) if _is_torch(scale_a) else _scales_np(scale_a, "scale_a").reshape(t * m, -1)
+        sb = scale_b.reshape(t * n, -1) if _is_torch(scale_b) else _scales_np(scale_b, "scale_b").reshape(t * n, -1)
+        if sa.shape[1] != sb.shape[1]:
+            raise ValueError(selected._scale_count_error)
+        if sparse_metadata is None and sa.shape[1] * desc.scale_block < k:
+            raise ValueError(selected._scale_cover_error)
+    elif scale_a is not None:
+        _scales_np(scale_a, "scale_a")
+        _scales_np(scale_b, "scale_b")
+    sparse, meta, flags = 0, None, 0
+    if sparse_metadata is not None:
+        if isinstance(sparse_metadata, (int, np.integer, list, tuple)):
+            sparse, meta, flags = _prepare(selected, a_format, scaling, kind, k, t * m, sparse_metadata)
+        else:
+            per_tile = sparse_metadata if _is_torch(sparse_metadata) else _words_np(sparse_metadata, "metadata")
+            sparse, meta, flags = _prepare(selected, a_format, scaling, kind, k, t, per_tile)
+            # one record per tile -> one record per A row of that tile
+            meta = meta.repeat_interleave(m, 0) if _is_torch(meta) else np.repeat(meta, m, axis=0)
+
+    def meta_error(first: int) -> None:
+        row = (first // (m * n)) * m + (first % (m * n)) // n
+        record = meta[0] if meta.shape[0] == 1 else meta[row]
+        words = np.asarray(record.cpu() if _is_torch(record) else record).astype(np.int64).tolist()
+        sparse_active_indices(a_format, k, words[0] if flags & nat.FLAG_META_REPEAT else words,
+                              kind="nvfp4" if (scaling or "").lower() == "ue4m3" else kind)
+
+    d = _run(selected, a_rows, b_rows, c_dev, k, dev, n=total, tile_m=m, tile_n=n, scale_a=sa, scale_b=sb,
+             sparse=sparse, meta=meta, flags=flags, a_compressed=False, check=check, meta_error=meta_error,
+             generic=generic)
+    if on_device:
+        return d.view(torch.uint32).reshape(t, m, n)
+    return d.cpu().numpy().view(np.uint32).reshape(t, m, n).copy()

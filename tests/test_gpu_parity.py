@@ -1,0 +1,351 @@
+"""Bit-exact parity of the CUDA emulator with the oracle and the reference's
+golden words, on a B200.
+
+Every comparison is raw-word equality (NaN payloads included).  Cases cover
+all 46 validation paths (golden reference outputs plus fresh seeds checked
+against the oracle), the frozen B200 vectors, ragged and edge-case K,
+special values, error behaviour, the matrix API, device-resident and packed
+inputs, and the benchmark configurations at full size through
+size-independent properties (fast kernel == generic kernel, shard
+invariance).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+import tcgen05_b200 as t5
+from conftest import full_desc
+from oracle import oracle
+from tcgen05_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+KEYS = ("a_format", "b_format", "d_type", "saturate", "scaling", "scale_vec", "kind")
+
+
+def gpu_cases(cases, **kw):
+    d = full_desc(cases.desc)
+    return t5.mma_dot_batch(cases.a, cases.b, cases.c, scale_a=cases.scale_a, scale_b=cases.scale_b,
+                            sparse_metadata=cases.meta, **{k: d[k] for k in KEYS}, **kw)
+
+
+def assert_words_equal(got, want, label=""):
+    got = np.asarray(got, dtype=np.uint32)
+    want = np.asarray(want, dtype=np.uint32)
+    bad = np.flatnonzero(got != want)
+    assert bad.size == 0, (f"{label}: {bad.size} of {want.size} words differ; first case {bad[0]}: "
+                           f"got 0x{int(got[bad[0]]):08x} want 0x{int(want[bad[0]]):08x}")
+
+
+@pytest.mark.parametrize("spec", workloads.validation_paths(), ids=lambda s: s.name)
+def test_path_matches_reference_words(spec, golden_paths):
+    index, arrays = golden_paths
+    entry = index["paths"][spec.name]
+    cases = workloads.path_cases(spec, entry["n"])
+    assert cases.digest() == entry["sha256"]
+    assert_words_equal(gpu_cases(cases), arrays[f"path:{spec.name}"], spec.name)
+
+
+@pytest.mark.parametrize("spec", workloads.validation_paths(), ids=lambda s: s.name)
+def test_path_matches_oracle_fresh_seed(spec):
+    cases = workloads.path_cases(spec, 1 << 15, seed=spec.seed + 7777)
+    want = oracle.eval_cases(cases)
+    assert_words_equal(gpu_cases(cases), want, spec.name)
+    assert_words_equal(gpu_cases(cases, generic=True), want, spec.name + " (generic kernel)")
+
+
+def test_frozen_b200_vectors(validation_vectors):
+    for v in validation_vectors["vectors"]:
+        d = full_desc(v["desc"])
+        model = t5.make_model(d["a_format"], d["b_format"], d_type=d["d_type"], saturate=d["saturate"],
+                              scaling=d["scaling"], scale_vec=d["scale_vec"], kind=d["kind"])
+        sa = None if v["scale_a"] is None else tuple(v["scale_a"])
+        sb = None if v["scale_b"] is None else tuple(v["scale_b"])
+        case = t5.DotProduct(tuple(v["a"]), tuple(v["b"]), v["c"], sa, sb)
+        assert model.eval(case) == v["expected"], v["name"]
+        assert model.matches(case, v["expected"])
+
+
+def test_frozen_public_api_calls(validation_vectors):
+    for call in validation_vectors["public_calls"]:
+        kw = dict(call["kwargs"])
+        if call["api"] == "mma_dot":
+            if isinstance(kw.get("sparse_metadata"), list):
+                kw["sparse_metadata"] = tuple(kw["sparse_metadata"])
+            assert t5.mma_dot(**kw) == call["result"], call
+        else:
+            got = t5.mma(**kw)
+            assert [list(r) for r in got] == call["result"]
+
+
+def test_validation_suite_replay():
+    """The reference's validate() flow (validation.py:227-344) through this
+    package: model vectors via eval_many in one launch per descriptor."""
+    import json
+
+    from conftest import GOLDEN
+
+    vv = json.loads((GOLDEN / "validation_vectors.json").read_text())["vectors"]
+    groups = {}
+    for v in vv:
+        key = tuple(sorted(full_desc(v["desc"]).items()))
+        groups.setdefault(key, []).append(v)
+    for key, vs in groups.items():
+        d = dict(key)
+        model = t5.make_model(d["a_format"], d["b_format"], d_type=d["d_type"], saturate=d["saturate"],
+                              scaling=d["scaling"], scale_vec=d["scale_vec"], kind=d["kind"])
+        cases = [t5.DotProduct(tuple(v["a"]), tuple(v["b"]), v["c"],
+                               None if v["scale_a"] is None else tuple(v["scale_a"]),
+                               None if v["scale_b"] is None else tuple(v["scale_b"])) for v in vs]
+        got = model.eval_many(cases)
+        assert got.tolist() == [v["expected"] for v in vs]
+
+
+@pytest.mark.parametrize("name", ["tf32-k8", "e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "mx-e2m3xe3m2-k32",
+                                  "u8xs8-k32-sat", "u8xs8-k32-wrap", "nvfp4-k64", "nvfp4-sparse-k128"])
+def test_configurations_match_reference_and_oracle(name, golden_paths):
+    index, arrays = golden_paths
+    entry = index["configs"][name]
+    cases = workloads.config_cases(name, entry["n"], entry["seed"])
+    assert_words_equal(gpu_cases(cases), arrays[f"config:{name}"], name)
+    big = workloads.config_cases(name, 1 << 17, seed=99)
+    assert_words_equal(gpu_cases(big), oracle.eval_cases(big), name + " 2^17 vs oracle")
+
+
+# ------------------------------------------------------------ edge cases
+
+EDGE_DESCS = [
+    dict(a_format="tf32"), dict(a_format="bf16"), dict(a_format="f16"), dict(a_format="f16", d_type="f16"),
+    dict(a_format="e4m3"), dict(a_format="e5m2"), dict(a_format="e2m3"), dict(a_format="e3m2"),
+    dict(a_format="e2m1"), dict(a_format="e4m3", b_format="e5m2"), dict(a_format="e5m2", b_format="e2m1", d_type="f16"),
+    dict(a_format="e3m2", b_format="e2m3", d_type="f16"),
+    dict(a_format="u8", b_format="s8", d_type="s32"), dict(a_format="s8", d_type="s32", saturate=True),
+    dict(a_format="e2m1", scaling="ue4m3"), dict(a_format="e4m3", scaling="ue8m0"),
+    dict(a_format="e5m2", b_format="e2m3", scaling="ue8m0"), dict(a_format="e2m1", scaling="ue8m0", kind="mxf8f6f4"),
+    dict(a_format="e2m1", scaling="ue8m0", kind="mxf4"), dict(a_format="e2m1", scaling="ue8m0", kind="mxf4nvf4"),
+    dict(a_format="e2m1", scaling="ue8m0", kind="mxf4nvf4", scale_vec=4),
+]
+
+
+def _edge_words(fmt, rng, n, k):
+    """Words biased toward special encodings: zeros, subnormals, max, Inf/NaN."""
+    w = workloads.format_words(fmt if fmt != "fp8" else "e4m3", rng, n * k).reshape(n, k)
+    special = {
+        "tf32": [0, 0x80000000, 0x00002000, 0x7F800000, 0xFF800000, 0x7FC00000, 0x7F800001, 0x7F7FFFFF, 0x3F800000],
+        "bf16": [0, 0x80000000, 0x00010000, 0x7F800000, 0xFF800000, 0x7FC00000, 0x7F80FFFF, 0x7F7F0000],
+        "f16": [0, 0x8000, 0x0001, 0x7C00, 0xFC00, 0x7E00, 0x7BFF, 0x3C00],
+        "e4m3": [0, 0x80, 0x01, 0x7F, 0xFF, 0x7E, 0x38],
+        "e5m2": [0, 0x80, 0x01, 0x7C, 0xFC, 0x7F, 0x7B, 0x3C],
+        "e2m3": [0, 0x20, 0x01, 0x1F, 0x3F, 0x08],
+        "e3m2": [0, 0x20, 0x01, 0x1F, 0x3F, 0x0C],
+        "e2m1": [0, 8, 1, 7, 15, 2],
+        "u8": [0, 1, 0x7F, 0x80, 0xFF],
+        "s8": [0, 1, 0x7F, 0x80, 0xFF],
+    }[fmt]
+    pick = rng.random((n, k)) < 0.35
+    choice = np.array(special, dtype=np.uint32)[rng.integers(0, len(special), size=(n, k))]
+    return np.where(pick, choice, w).astype(np.uint32)
+
+
+@pytest.mark.parametrize("desc", EDGE_DESCS, ids=lambda d: "-".join(str(v) for v in d.values()))
+@pytest.mark.parametrize("k", [1, 2, 3, 5, 8, 16, 17, 31, 32, 33, 48, 64, 96, 127, 128, 256])
+def test_edge_values_and_ragged_k(desc, k):
+    d = full_desc(desc)
+    rng = np.random.Generator(np.random.PCG64(k * 131 + len(str(desc))))
+    n = 4096
+    a_fmt = t5.normalize_format(d["a_format"])
+    b_fmt = t5.normalize_format(d["b_format"] or d["a_format"])
+    a = _edge_words(a_fmt, rng, n, k)
+    b = _edge_words(b_fmt, rng, n, k)
+    c_special = np.array([0, 0x80000000, 0x7F800000, 0xFF800000, 0x7FC00000, 0x00000001, 0x7F7FFFFF, 0x3F800000],
+                         dtype=np.uint32)
+    c = np.where(rng.random(n) < 0.3, c_special[rng.integers(0, 8, n)], workloads.f32_words(rng, n))
+    if d["d_type"] == "f16":
+        c = np.where(rng.random(n) < 0.3, np.array([0, 0x8000, 0x7C00, 0xFC00, 0x7E00, 1, 0x7BFF],
+                                                   dtype=np.uint32)[rng.integers(0, 7, n)],
+                     workloads.f16_words(rng, n)).astype(np.uint32)
+    sa = sb = None
+    if d["scaling"] is not None:
+        block = 16 if (d["scaling"] == "ue4m3" or d["scale_vec"] == 4) else 32
+        nb = (k + block - 1) // block
+        top = 0x80 if d["scaling"] == "ue4m3" else 0x100
+        sa = rng.integers(0, top, size=(n, nb), dtype=np.uint32).astype(np.uint8)
+        sb = rng.integers(0, top, size=(n, nb), dtype=np.uint32).astype(np.uint8)
+        # mostly near-unit scales, with the full range (NaN encodings included) mixed in
+        unit = 0x38 if d["scaling"] == "ue4m3" else 0x7F
+        near = rng.random((n, nb)) < 0.6
+        sa = np.where(near, unit + rng.integers(-3, 4, size=(n, nb)), sa).astype(np.uint8)
+        sb = np.where(near, unit + rng.integers(-3, 4, size=(n, nb)), sb).astype(np.uint8)
+    want, st = oracle.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, **{kk: d[kk] for kk in KEYS})
+    assert (st == 0).all()
+    got = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, **{kk: d[kk] for kk in KEYS})
+    assert_words_equal(got, want, f"{desc} K={k}")
+
+
+SPARSE_DESCS = [
+    dict(a_format="tf32"), dict(a_format="bf16"), dict(a_format="f16", d_type="f16"), dict(a_format="e4m3"),
+    dict(a_format="e2m1", b_format="e4m3"), dict(a_format="u8", b_format="s8", d_type="s32", saturate=True),
+    dict(a_format="e2m1", scaling="ue4m3"), dict(a_format="e3m2", scaling="ue8m0"),
+    dict(a_format="e2m1", scaling="ue8m0", kind="mxf4"), dict(a_format="e2m1", scaling="ue8m0", kind="mxf4nvf4",
+                                                              scale_vec=4),
+]
+
+
+@pytest.mark.parametrize("desc", SPARSE_DESCS, ids=lambda d: "-".join(str(v) for v in d.values()))
+@pytest.mark.parametrize("k", [2, 7, 16, 30, 64, 100, 128])
+@pytest.mark.parametrize("form", ["int", "words"])
+def test_sparse_selection_matches_oracle(desc, k, form):
+    d = full_desc(desc)
+    rng = np.random.Generator(np.random.PCG64(1000 + k))
+    n = 2048
+    a_fmt = t5.normalize_format(d["a_format"])
+    b_fmt = t5.normalize_format(d["b_format"] or d["a_format"])
+    a = _edge_words(a_fmt, rng, n, k)
+    b = _edge_words(b_fmt, rng, n, k)
+    c = workloads.f32_words(rng, n) if d["d_type"] != "f16" else workloads.f16_words(rng, n)
+    sel = workloads.SELECTORS_TF32 if a_fmt == "tf32" else workloads.SELECTORS_2OF4
+    words = 8  # enough nibbles for TF32 at K=128
+    meta = np.stack([workloads.metadata_words(rng, n, sel) for _ in range(words)], axis=1)
+    if form == "int":
+        meta = meta[:, :1]
+    sa = sb = None
+    if d["scaling"] is not None:
+        top = 0x80 if d["scaling"] == "ue4m3" else 0x100
+        sa = rng.integers(0, top, size=(n, 8), dtype=np.uint32).astype(np.uint8)
+        sb = rng.integers(0, top, size=(n, 8), dtype=np.uint32).astype(np.uint8)
+    want, st = oracle.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta,
+                                    meta_is_int=form == "int", **{kk: d[kk] for kk in KEYS})
+    ok = st == 0
+    got = t5.mma_dot_batch(a[ok], b[ok], c[ok], scale_a=None if sa is None else sa[ok],
+                           scale_b=None if sb is None else sb[ok],
+                           sparse_metadata=meta[ok, 0] if form == "int" else meta[ok], **{kk: d[kk] for kk in KEYS})
+    assert_words_equal(got, want[ok], f"sparse {desc} K={k} {form}")
+
+
+def test_sparse_errors_match_reference_messages():
+    a = np.full((3, 16), 0x3F800000, dtype=np.uint32)
+    with pytest.raises(ValueError, match=r"illegal sparse selector 0x5 in chunk 3"):
+        t5.mma_dot_batch(a, a, a_format="tf32", sparse_metadata=np.array([0x44444444, 0x44445444, 0x44444444]))
+    assert t5.mma_dot(a[0], a[0], a_format="tf32", sparse_metadata=0x44444444) == 0x41000000
+    e = np.full((1, 128), 2, dtype=np.uint32)
+    with pytest.raises(ValueError, match="16 metadata nibbles are required for K=128"):
+        t5.mma_dot_batch(e, e, a_format="e2m1", scaling="ue4m3", sparse_metadata=np.array([[0x44444444]]))
+
+
+def test_scale_errors_match_reference_messages():
+    e = np.ones((2, 64), dtype=np.uint32)
+    with pytest.raises(ValueError, match="NVFP4 A/B scale block counts differ"):
+        t5.mma_dot_batch(e, e, a_format="e2m1", scaling="ue4m3", scale_a=np.full((2, 3), 0x38),
+                         scale_b=np.full((2, 4), 0x38))
+    with pytest.raises(ValueError, match="NVFP4 case has more K values than scale blocks cover"):
+        t5.mma_dot(tuple(range(16)) * 4, (1,) * 64, a_format="e2m1", scaling="ue4m3", scale_a=(0x38,) * 3,
+                   scale_b=(0x38,) * 3)
+    with pytest.raises(ValueError, match="^case has more K values than scale blocks cover"):
+        t5.mma_dot((1,) * 64, (1,) * 64, a_format="e2m1", scaling="ue8m0", kind="mxf4", scale_a=(0x7F,),
+                   scale_b=(0x7F,))
+
+
+# ------------------------------------------------------------- matrix API
+
+
+def test_matrix_tile_matches_reference(golden_paths):
+    index, arrays = golden_paths
+    a, b, c, d = arrays["matrix:a"], arrays["matrix:b"], arrays["matrix:c"], arrays["matrix:d"]
+    got = t5.mma(a.tolist(), b.tolist(), c.tolist(), a_format=index["matrix"]["a_format"])
+    assert np.array_equal(np.array(got, dtype=np.uint32), d)
+
+
+@pytest.mark.parametrize("desc", [dict(a_format="bf16"), dict(a_format="e2m1", scaling="ue4m3"),
+                                  dict(a_format="e4m3", b_format="e2m1", d_type="f16"),
+                                  dict(a_format="u8", d_type="s32", saturate=True)])
+def test_batched_tiles_match_oracle(desc):
+    d = full_desc(desc)
+    rng = np.random.Generator(np.random.PCG64(77))
+    t, m, n, k = 6, 24, 40, 64 if d["scaling"] else 16
+    a_fmt = t5.normalize_format(d["a_format"])
+    b_fmt = t5.normalize_format(d["b_format"] or d["a_format"])
+    a = _edge_words(a_fmt, rng, t * m, k).reshape(t, m, k)
+    bt = _edge_words(b_fmt, rng, t * n, k).reshape(t, n, k)
+    b = bt.transpose(0, 2, 1).copy()
+    c = (workloads.f16_words(rng, t * m * n) if d["d_type"] == "f16" else workloads.f32_words(rng, t * m * n))
+    c = c.reshape(t, m, n)
+    sa = sb = None
+    if d["scaling"]:
+        sa = rng.integers(0x30, 0x40, size=(t, m, 4), dtype=np.uint32).astype(np.uint8)
+        sb = rng.integers(0x30, 0x40, size=(t, n, 4), dtype=np.uint32).astype(np.uint8)
+    got = t5.mma_batch(a, b, c, scale_a=sa, scale_b=sb, **{kk: d[kk] for kk in KEYS})
+    aa = np.repeat(a, n, axis=1).reshape(-1, k)
+    bb = np.tile(bt, (1, m, 1)).reshape(-1, k)
+    saa = None if sa is None else np.repeat(sa, n, axis=1).reshape(-1, 4)
+    sbb = None if sb is None else np.tile(sb, (1, m, 1)).reshape(-1, 4)
+    want, st = oracle.mma_dot_batch(aa, bb, c.reshape(-1), scale_a=saa, scale_b=sbb, **{kk: d[kk] for kk in KEYS})
+    assert (st == 0).all()
+    assert_words_equal(got.reshape(-1), want, str(desc))
+
+
+def test_matrix_sparse_shares_metadata():
+    rng = np.random.Generator(np.random.PCG64(5))
+    a = rng.integers(0, 256, size=(8, 64), dtype=np.uint32)
+    b = rng.integers(0, 256, size=(64, 12), dtype=np.uint32)
+    got = t5.mma(a.tolist(), b.tolist(), a_format="e4m3", sparse_metadata=(0x4C8D9E64, 0xE6D9C844))
+    for i in range(8):
+        for j in range(12):
+            assert got[i][j] == t5.mma_dot(a[i].tolist(), b[:, j].tolist(), a_format="e4m3",
+                                           sparse_metadata=(0x4C8D9E64, 0xE6D9C844))
+
+
+# ------------------------------------------------------ device-side inputs
+
+
+def test_device_tensors_and_packed_rows():
+    import torch
+
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import packing
+
+    cases = workloads.config_cases("nvfp4-sparse-k128", 8192, seed=3)
+    want = oracle.eval_cases(cases)
+    dev = torch.device("cuda")
+    a = torch.from_numpy(cases.a.view(np.int32)).to(dev)
+    b = torch.from_numpy(cases.b.view(np.int32)).to(dev)
+    c = torch.from_numpy(cases.c.view(np.int32)).to(dev)
+    meta = torch.from_numpy(cases.meta.view(np.int32)).to(dev)
+    sa = torch.from_numpy(cases.scale_a).to(dev)
+    sb = torch.from_numpy(cases.scale_b).to(dev)
+    got = t5.mma_dot_batch(a, b, c, a_format="e2m1", scaling="ue4m3", scale_a=sa, scale_b=sb, sparse_metadata=meta)
+    assert got.is_cuda
+    assert_words_equal(got.cpu().numpy(), want, "device words")
+    # compressed A (only the selected elements), as sparse hardware stores it
+    act = workloads.active_mask(cases.meta, 128, "4of8")
+    comp = cases.a[act].reshape(cases.n, 64)
+    pa = t5.PackedRows(torch.from_numpy(packing.pack_rows(comp, nat.FMT_E2M1)).to(dev), 64, compressed=True)
+    pb = t5.PackedRows(torch.from_numpy(packing.pack_rows(cases.b, nat.FMT_E2M1)).to(dev), 128)
+    got2 = t5.mma_dot_batch(pa, pb, c, a_format="e2m1", scaling="ue4m3", scale_a=sa, scale_b=sb,
+                            sparse_metadata=meta)
+    assert_words_equal(got2.cpu().numpy(), want, "compressed A")
+    # device packing kernel == host packing
+    for fmt in range(10):
+        words = torch.from_numpy(cases.b[:64].view(np.int32)).to(dev)
+        host = packing.pack_rows(cases.b[:64], fmt)
+        assert np.array_equal(packing.pack_rows_device(words, fmt).cpu().numpy(), host)
+
+
+@pytest.mark.parametrize("name", ["e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "nvfp4-k64", "u8xs8-k32-sat",
+                                  "mx-e2m3xe3m2-k32", "tf32-k8"])
+def test_full_size_fast_equals_generic_and_shards(name):
+    """Size-independent properties at the configuration's full size: the
+    dispatching entry point equals the generic kernel word for word, and a
+    sharded evaluation equals the whole-batch one."""
+    n = {"tf32-k8": 65536, "e4m3xe5m2-k32": 1 << 20, "e4m3xe5m2-k32-f16": 1 << 20, "mx-e2m3xe3m2-k32": 1 << 22,
+         "u8xs8-k32-sat": 1 << 22, "nvfp4-k64": 1 << 22}[name]
+    cases = workloads.config_cases(name, n, seed=11)
+    fast = gpu_cases(cases)
+    generic = gpu_cases(cases, generic=True)
+    assert_words_equal(fast, generic, name + " fast vs generic")
+    half = cases.n // 3
+    parts = np.concatenate([gpu_cases(cases.subset(slice(0, half))), gpu_cases(cases.subset(slice(half, None)))])
+    assert_words_equal(parts, fast, name + " shards")
+    sample = np.random.Generator(np.random.PCG64(1)).choice(cases.n, 20000, replace=False)
+    assert_words_equal(fast[sample], oracle.eval_cases(cases.subset(sample)), name + " sample vs oracle")

@@ -1,0 +1,148 @@
+"""Pin the CPU oracle (oracle/t5e_oracle.c) to the reference.
+
+The oracle is the parity checker of the CUDA emulator, so before any GPU
+result is compared with it, it must reproduce the reference exactly:
+
+* the frozen B200 words of tcgen05_model/validation.py:37-344 and the
+  hardware vectors of the reference's tests/test_model.py:141-169;
+* the reference's outputs on seeded cases of all 46 validation paths and of
+  the benchmark configurations (tests/golden/paths.npz, made by
+  tests/golden/make_golden.py from the reference itself);
+* the reference's make_model legality decisions and sparse_active_indices.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import full_desc
+from oracle import oracle
+from tcgen05_b200 import workloads
+
+ORACLE_KEYS = ("a_format", "b_format", "d_type", "saturate", "scaling", "scale_vec", "kind")
+
+
+def _oracle_one(desc, a, b, c, scale_a=None, scale_b=None, meta=None, meta_is_int=False):
+    d = full_desc(desc)
+    kw = {k: d[k] for k in ORACLE_KEYS}
+    out, st = oracle.mma_dot_batch(
+        np.array([a], dtype=np.uint32), np.array([b], dtype=np.uint32), np.array([c], dtype=np.uint32),
+        scale_a=None if scale_a is None else np.array([scale_a]), scale_b=None if scale_b is None else np.array([scale_b]),
+        sparse_metadata=None if meta is None else np.array([meta if isinstance(meta, list) else [meta]]),
+        meta_is_int=meta_is_int, threads=1, **kw)
+    return int(out[0]), int(st[0])
+
+
+def test_frozen_b200_vectors(validation_vectors):
+    vectors = validation_vectors["vectors"]
+    assert len(vectors) >= 60
+    for v in vectors:
+        word, st = _oracle_one(v["desc"], v["a"], v["b"], v["c"], v["scale_a"], v["scale_b"])
+        assert st == 0, v["name"]
+        assert word == v["expected"] == v["reference"], (v["name"], hex(word), hex(v["expected"]))
+
+
+def _public_call(kwargs):
+    kw = dict(kwargs)
+    a, b = kw.pop("a"), kw.pop("b")
+    c = kw.pop("c", 0)
+    meta = kw.pop("sparse_metadata", None)
+    sa, sb = kw.pop("scale_a", None), kw.pop("scale_b", None)
+    desc = {k: kw[k] for k in ORACLE_KEYS if k in kw}
+    meta_is_int = isinstance(meta, int)
+    return _oracle_one(desc, a, b, c, sa, sb, meta, meta_is_int)
+
+
+def test_frozen_public_api_calls(validation_vectors):
+    calls = validation_vectors["public_calls"]
+    assert len(calls) >= 30
+    for call in calls:
+        if call["api"] == "mma_dot":
+            word, st = _public_call(call["kwargs"])
+            assert st == 0
+            assert word == call["result"], call
+        else:
+            kw = dict(call["kwargs"])
+            a, b = kw.pop("a"), kw.pop("b")
+            c = kw.pop("c", None)
+            for i, row in enumerate(a):
+                for j in range(len(b[0])):
+                    col = [b[k][j] for k in range(len(b))]
+                    cw = 0 if c is None else c[i][j]
+                    word, st = _public_call(dict(kw, a=row, b=col, c=cw))
+                    assert st == 0 and word == call["result"][i][j]
+
+
+@pytest.mark.parametrize("spec", workloads.validation_paths(), ids=lambda s: s.name)
+def test_validation_path_fixtures(spec, golden_paths):
+    index, arrays = golden_paths
+    entry = index["paths"][spec.name]
+    cases = workloads.path_cases(spec, entry["n"])
+    assert cases.digest() == entry["sha256"], "case generator output changed; regenerate the fixtures"
+    got = oracle.eval_cases(cases, threads=2)
+    want = arrays[f"path:{spec.name}"]
+    mism = np.flatnonzero(got != want)
+    assert mism.size == 0, f"{spec.name}: {mism.size} mismatches, first case {mism[:1]}"
+
+
+@pytest.mark.parametrize("name", ["tf32-k8", "e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "mx-e2m3xe3m2-k32",
+                                  "u8xs8-k32-sat", "u8xs8-k32-wrap", "nvfp4-k64", "nvfp4-sparse-k128"])
+def test_config_fixtures(name, golden_paths):
+    index, arrays = golden_paths
+    entry = index["configs"][name]
+    cases = workloads.config_cases(name, entry["n"], entry["seed"])
+    assert cases.digest() == entry["sha256"]
+    got = oracle.eval_cases(cases, threads=2)
+    assert np.array_equal(got, arrays[f"config:{name}"])
+
+
+def test_matrix_tile_fixture(golden_paths):
+    index, arrays = golden_paths
+    a, b, c, d = arrays["matrix:a"], arrays["matrix:b"], arrays["matrix:c"], arrays["matrix:d"]
+    m, n = d.shape
+    aa = np.repeat(a, n, axis=0)
+    bb = np.tile(b.T, (m, 1))
+    got, st = oracle.mma_dot_batch(aa, bb, c.reshape(-1), a_format=index["matrix"]["a_format"])
+    assert (st == 0).all()
+    assert np.array_equal(got.reshape(m, n), d)
+
+
+def test_descriptor_grid(descriptor_grid):
+    for rec in descriptor_grid:
+        kw = {k: rec[k] for k in ORACLE_KEYS}
+        st = oracle.check_descriptor(**kw)
+        assert (st == 0) == rec["ok"], rec
+
+
+def test_sparse_active(sparse_records):
+    import ctypes
+
+    lib = oracle.load()
+    kinds = {None: 0, "mxf8f6f4": 1, "mxf4": 2, "mxf4nvf4": 3, "nvfp4": 4}
+    for rec in sparse_records:
+        meta = rec["metadata"]
+        words = np.array([meta] if isinstance(meta, int) else meta, dtype=np.uint32)
+        active = np.zeros(rec["k"], dtype=np.uint8)
+        st = lib.oracle_sparse_active(oracle.FORMATS[oracle.ALIASES.get(rec["format"], rec["format"])], rec["k"],
+                                      words.ctypes.data, words.size, 1 if isinstance(meta, int) else 0,
+                                      kinds.get(rec["kind"], 99), 0, active.ctypes.data_as(ctypes.c_void_p))
+        if "error" in rec:
+            assert st != 0, rec
+        else:
+            assert st == 0, rec
+            assert sorted(np.flatnonzero(active).tolist()) == rec["active"], rec
+
+
+def test_oracle_reports_error_cases():
+    # illegal selector, too few metadata words, scale count mismatch, scale coverage
+    a = np.ones((1, 16), dtype=np.uint32) * 0x3F800000
+    _, st = oracle.mma_dot_batch(a, a, sparse_metadata=np.array([[0x44444445]]), a_format="tf32")
+    assert st[0] == -4
+    e = np.ones((1, 64), dtype=np.uint32)
+    _, st = oracle.mma_dot_batch(e, e, scale_a=np.full((1, 3), 0x38), scale_b=np.full((1, 4), 0x38),
+                                 a_format="e2m1", scaling="ue4m3")
+    assert st[0] == -7
+    _, st = oracle.mma_dot_batch(e, e, scale_a=np.full((1, 3), 0x38), scale_b=np.full((1, 3), 0x38),
+                                 a_format="e2m1", scaling="ue4m3")
+    assert st[0] == -8
