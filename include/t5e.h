@@ -155,6 +155,7 @@ typedef struct t5e_batch {
 #define T5E_CASE_EMPTY 2          /* no element selected, model.py:35-36 */
 #define T5E_CASE_SCALE_COVER 3    /* more K than scale blocks cover, model.py:730-731, 857-858 */
 #define T5E_CASE_META_WORDS 4     /* too few metadata nibbles, simulator.py:60-61 */
+#define T5E_CASE_TIMEOUT 5        /* a bounded device wait for the case's input copy expired (no result) */
 
 /* library ABI version (T5E_ABI_VERSION) */
 int t5e_abi_version(void);

@@ -51,7 +51,7 @@ ERR_CUDA = -3
 ERR_K_RANGE = -4
 MAX_K = 65536
 
-CASE_OK, CASE_BAD_SELECTOR, CASE_EMPTY, CASE_SCALE_COVER, CASE_META_WORDS = 0, 1, 2, 3, 4
+CASE_OK, CASE_BAD_SELECTOR, CASE_EMPTY, CASE_SCALE_COVER, CASE_META_WORDS, CASE_TIMEOUT = 0, 1, 2, 3, 4, 5
 
 
 class Model(ctypes.Structure):

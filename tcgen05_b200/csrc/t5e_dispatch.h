@@ -15,6 +15,9 @@ int launch_fast(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 // Records the last launch error for t5e_last_error(); T5E_OK or T5E_ERR_CUDA.
 int kernel_status(const char* what);
 
+// Records a failing CUDA call for t5e_last_error().
+void set_cuda_error(const char* what, cudaError_t err);
+
 // Grid size for a grid-stride loop over n items.
 int grid_for(uint64_t n, int block);
 

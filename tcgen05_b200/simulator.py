@@ -215,6 +215,8 @@ def _raise_case_status(model, status: int, *, meta_message=None) -> None:
         raise ValueError(model._scale_cover_error)
     if status in (nat.CASE_BAD_SELECTOR, nat.CASE_META_WORDS) and meta_message is not None:
         meta_message()
+    if status == nat.CASE_TIMEOUT:
+        raise RuntimeError("a bounded device wait for this case's input copy expired; no result was produced")
     raise ValueError(f"invalid case (status {status})")
 
 
