@@ -58,18 +58,23 @@ def measured_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def profiled_traffic(kernel_tag: str):
-    """dram bytes per launch of the dominant kernel from the committed ncu
-    summary (a line 'traffic_bytes_per_launch[<tag>]: <bytes>'), or None."""
+def profiled_figure(name: str, kernel_tag: str):
+    """A figure of the dominant kernel from the committed ncu summaries (a line
+    '<name>[<tag>]: <number>'), or None.  Used for the DRAM traffic per launch
+    ('traffic_bytes_per_launch') and the ALU-pipe utilisation ('alu_pipe_pct')."""
+    key = f"{name}[{kernel_tag}]:"
     for f in sorted((REPO / "profiles").glob("*.md")) + sorted((REPO / "profiles").glob("*.txt")):
         for line in f.read_text().splitlines():
-            key = f"traffic_bytes_per_launch[{kernel_tag}]:"
             if line.strip().startswith(key):
                 try:
                     return float(line.split(":", 1)[1].split()[0])
                 except ValueError:
                     return None
     return None
+
+
+def _pct(x):
+    return None if x is None else x / 100.0
 
 
 # ------------------------------------------------------------------ clocks
@@ -300,9 +305,13 @@ def run_ours(args) -> int:
             "gpu_launches": args.steps * len(VARIANTS),
             "kernel_ms": {v: statistics.mean(ms) for v, ms in launch_ms.items()},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                         "frac": achieved / peaks["hbm_gbs"], "traffic": profiled_traffic(dom),
+                         "frac": achieved / peaks["hbm_gbs"],
+                         "traffic": profiled_figure("traffic_bytes_per_launch", dom),
                          "kernel": f"t5e raw-window kernel, {dom}", "peak_source": f"{peak_kind} hbm_gbs",
-                         "algorithmic_bytes_per_launch": bytes_per_launch},
+                         "algorithmic_bytes_per_launch": bytes_per_launch,
+                         "int_pipe": {"alu_pipe_frac": _pct(profiled_figure("alu_pipe_pct", dom)),
+                                      "source": "ncu sm__pipe_alu_cycles_active.avg.pct_of_peak_sustained_active, committed profile"},
+                         "binds": "integer issue (ALU pipe); HBM fraction reported for the contract"},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps},
             "clocks": clocks,
@@ -394,8 +403,8 @@ def run_reference(args) -> int:
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=4000)
-    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=20000)
+    ap.add_argument("--warmup", type=int, default=200)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--cases", type=int, default=1 << 20, help="cases per variant per GPU (default 2^20)")
     ap.add_argument("--e2e-steps", type=int, default=20)

@@ -155,7 +155,8 @@ typedef struct t5e_batch {
 #define T5E_CASE_EMPTY 2          /* no element selected, model.py:35-36 */
 #define T5E_CASE_SCALE_COVER 3    /* more K than scale blocks cover, model.py:730-731, 857-858 */
 #define T5E_CASE_META_WORDS 4     /* too few metadata nibbles, simulator.py:60-61 */
-#define T5E_CASE_TIMEOUT 5        /* a bounded device wait for the case's input copy expired (no result) */
+#define T5E_CASE_TIMEOUT 5        /* reserved for kernels with bounded device waits (no result word);
+                                     no kernel of this library waits, so none sets it today */
 
 /* library ABI version (T5E_ABI_VERSION) */
 int t5e_abi_version(void);
