@@ -80,6 +80,15 @@ def _pct(x):
 # ------------------------------------------------------------------ clocks
 
 
+def smi_gpu_id(local: int) -> str:
+    """nvidia-smi's id (index or UUID) of this process's CUDA device `local`,
+    following CUDA_VISIBLE_DEVICES when it remaps devices."""
+    vis = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    if local < len(vis):
+        return vis[local]
+    return str(local)
+
+
 class ClockSampler:
     """nvidia-smi clock/throttle samples during the timed region."""
 
@@ -87,8 +96,8 @@ class ClockSampler:
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
+    def __init__(self, gpu_id: str):
+        self.gpu = gpu_id
         self.proc = None
         self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"t5e_clocks_{os.getpid()}.csv"
 
@@ -197,7 +206,7 @@ def run_ours(args) -> int:
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(2 * len(VARIANTS))] for _ in range(args.steps)]
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local if "CUDA_VISIBLE_DEVICES" not in os.environ else local)
+    sampler = ClockSampler(smi_gpu_id(local))
     sampler.start()
     time.sleep(0.3)
     if world > 1:

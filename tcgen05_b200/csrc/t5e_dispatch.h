@@ -12,6 +12,9 @@ namespace t5e {
 // T5E_ERR_UNSUPPORTED (and launches nothing) otherwise.
 int launch_fast(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 
+// The NVFP4 kernel (t5e_nvfp4.cu); same contract as launch_fast.
+int launch_nvfp4(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
+
 // Records the last launch error for t5e_last_error(); T5E_OK or T5E_ERR_CUDA.
 int kernel_status(const char* what);
 

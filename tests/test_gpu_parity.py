@@ -332,14 +332,68 @@ def test_device_tensors_and_packed_rows():
         assert np.array_equal(packing.pack_rows_device(words, fmt).cpu().numpy(), host)
 
 
-@pytest.mark.parametrize("name", ["e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "nvfp4-k64", "u8xs8-k32-sat",
-                                  "mx-e2m3xe3m2-k32", "tf32-k8"])
+def _nvfp4_adversarial(rng, n, sparse):
+    """NVFP4 cases aimed at the kernel's regime boundaries: scale pairs far
+    apart (blocks 28 binades below the window), zero and NaN scales, C
+    exponents inside the band where the element exponents decide dominance,
+    zero/subnormal/special C and, for the sparse form, illegal selectors."""
+    k = 128 if sparse else 64
+    a = rng.integers(0, 16, size=(n, k), dtype=np.uint32)
+    b = rng.integers(0, 16, size=(n, k), dtype=np.uint32)
+    a = np.where(rng.random((n, k)) < 0.4, a & 8, a).astype(np.uint32)
+    extremes = np.array([0x01, 0x02, 0x07, 0x08, 0x7E, 0x77, 0x40, 0x38, 0x00, 0x80, 0x7F, 0xFF, 0xFE], dtype=np.uint8)
+    pick = rng.random((n, 4)) < 0.7
+    sa = np.where(pick, extremes[rng.integers(0, len(extremes), (n, 4))], rng.integers(0, 256, (n, 4))).astype(np.uint8)
+    sb = np.where(pick, extremes[rng.integers(0, len(extremes), (n, 4))], rng.integers(0, 256, (n, 4))).astype(np.uint8)
+    c = ((rng.integers(0, 2, n).astype(np.uint32) << 31) | (rng.integers(100, 160, n).astype(np.uint32) << 23)
+         | rng.integers(0, 1 << 23, n).astype(np.uint32))
+    special = np.array([0, 0x80000000, 0x00000001, 0x807FFFFF, 0x7F800000, 0xFF800000, 0x7FC00000, 0x7F7FFFFF],
+                       dtype=np.uint32)
+    c = np.where(rng.random(n) < 0.2, special[rng.integers(0, len(special), n)], c).astype(np.uint32)
+    meta = None
+    if sparse:
+        sel = np.array([4, 8, 0xC, 9, 0xD, 6, 0xE], dtype=np.uint32)
+        lo = workloads.metadata_words(rng, n, sel)
+        hi = workloads.metadata_words(rng, n, sel)
+        flip = rng.random(n) < 0.1
+        lo = np.where(flip, lo ^ (rng.integers(1, 16, n).astype(np.uint32) << (4 * rng.integers(0, 8, n).astype(np.uint32))),
+                      lo).astype(np.uint32)
+        meta = np.stack([lo, hi], axis=1)
+    return a, b, c, sa, sb, meta
+
+
+@pytest.mark.parametrize("sparse", [False, True])
+def test_nvfp4_kernel_regime_boundaries(sparse):
+    rng = np.random.Generator(np.random.PCG64(4242 + sparse))
+    n = 1 << 16
+    a, b, c, sa, sb, meta = _nvfp4_adversarial(rng, n, sparse)
+    kw = dict(a_format="e2m1", scaling="ue4m3", scale_vec=4)
+    want, st = oracle.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta, **kw)
+    ok = st == 0
+    assert ok.any()
+    got = t5.mma_dot_batch(a[ok], b[ok], c[ok], scale_a=sa[ok], scale_b=sb[ok],
+                           sparse_metadata=None if meta is None else meta[ok], **kw)
+    assert_words_equal(got, want[ok], f"nvfp4 sparse={sparse}")
+    if sparse:
+        # the illegal selectors raise the reference's ValueError, as the generic kernel does
+        bad = int(np.flatnonzero(~ok)[0])
+        with pytest.raises(ValueError):
+            t5.mma_dot_batch(a[bad:bad + 1], b[bad:bad + 1], c[bad:bad + 1], scale_a=sa[bad:bad + 1],
+                             scale_b=sb[bad:bad + 1], sparse_metadata=meta[bad:bad + 1], **kw)
+        fast = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta, check=False, **kw)
+        generic = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta, check=False,
+                                   generic=True, **kw)
+        assert_words_equal(fast, generic, "nvfp4 sparse fast vs generic (illegal selectors included)")
+
+
+@pytest.mark.parametrize("name", ["e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "nvfp4-k64", "nvfp4-sparse-k128",
+                                  "u8xs8-k32-sat", "mx-e2m3xe3m2-k32", "tf32-k8"])
 def test_full_size_fast_equals_generic_and_shards(name):
     """Size-independent properties at the configuration's full size: the
     dispatching entry point equals the generic kernel word for word, and a
     sharded evaluation equals the whole-batch one."""
     n = {"tf32-k8": 65536, "e4m3xe5m2-k32": 1 << 20, "e4m3xe5m2-k32-f16": 1 << 20, "mx-e2m3xe3m2-k32": 1 << 22,
-         "u8xs8-k32-sat": 1 << 22, "nvfp4-k64": 1 << 22}[name]
+         "u8xs8-k32-sat": 1 << 22, "nvfp4-k64": 1 << 22, "nvfp4-sparse-k128": 1 << 22}[name]
     cases = workloads.config_cases(name, n, seed=11)
     fast = gpu_cases(cases)
     generic = gpu_cases(cases, generic=True)
