@@ -325,6 +325,9 @@ def run_ours(args) -> int:
                     "steps": e2e_steps},
             "clocks": clocks,
         }
+        if world == 1 and not args.no_configs:
+            line["configs"] = measure_configs(torch, device, lib)
+            line["gpu_launches_configs"] = 23 * len(OTHER_CONFIGS)
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(sets, budget_s=args.cpu_seconds)
         print(json.dumps(line), flush=True)
@@ -332,6 +335,67 @@ def run_ours(args) -> int:
         dist.barrier()
         dist.destroy_process_group()
     return 0 if mismatches == 0 else 1
+
+
+OTHER_CONFIGS = ("tf32-k8", "mx-e2m3xe3m2-k32", "u8xs8-k32-sat", "u8xs8-k32-wrap", "nvfp4-k64",
+                 "nvfp4-sparse-k128", "matrix-bf16")
+
+
+def measure_configs(torch, device, lib, launches: int = 20, warmup: int = 3) -> dict:
+    """Every other benchmark configuration at its stated size, generated in
+    HBM: mean CUDA-event time of one launch of t5e_mma_dot_batch (L2 flushed
+    before each timed launch by writing a 256 MB buffer), element-MACs/s,
+    algorithmic GB/s and its fraction of the measured HBM peak, and the
+    number of result words that differ from the generic kernel on the first
+    2^18 cases."""
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import runtime, workloads
+
+    peaks, _ = measured_peaks()
+    stream = torch.cuda.current_stream(device)
+    handle = ctypes.c_void_p(stream.cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    out = {}
+    for idx, name in enumerate(OTHER_CONFIGS):
+        model, db = workloads.device_config(name, device, seed=1000 + idx)
+        desc = model.descriptor()
+        d = torch.empty(db.n, dtype=torch.int32, device=device)
+        bs = runtime.make_batch_struct(db, d, None)
+
+        def run(fn, s=bs):
+            rc = fn(ctypes.byref(desc), ctypes.byref(s), handle)
+            nat.check(rc, name)
+
+        for _ in range(warmup):
+            run(lib.t5e_mma_dot_batch)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(launches)]
+        for e0, e1 in ev:
+            flush.zero_()
+            e0.record(stream)
+            run(lib.t5e_mma_dot_batch)
+            e1.record(stream)
+        torch.cuda.synchronize(device)
+        us = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) * 1e3
+        # parity on a prefix: the dispatching entry point vs the generic kernel
+        per = db.tile_m * db.tile_n
+        m = min(db.n, max(per, (1 << 18) // per * per))
+        sub = runtime.make_batch_struct(db, d, None)
+        sub.n = m
+        gen = torch.empty(m, dtype=torch.int32, device=device)
+        sub_g = runtime.make_batch_struct(db, gen, None)
+        sub_g.n = m
+        run(lib.t5e_mma_dot_batch, sub)
+        run(lib.t5e_mma_dot_batch_generic, sub_g)
+        torch.cuda.synchronize(device)
+        mism = int((d[:m] != gen).sum().item())
+        macs, nbytes = workloads.config_work(name, db)
+        gbs = nbytes / (us * 1e-6) / 1e9
+        out[name] = {"cases": db.n, "k": db.k, "kernel_us": us, "value": macs / (us * 1e-6),
+                     "dot_products_per_s": db.n / (us * 1e-6), "algorithmic_gbs": gbs,
+                     "hbm_frac": gbs / peaks["hbm_gbs"], "mismatches_vs_generic": mism, "checked_cases": m}
+        del db, d, gen, bs, sub, sub_g
+        torch.cuda.empty_cache()
+    return out
 
 
 def cpu_baseline(sets, budget_s: float) -> dict:
@@ -419,6 +483,8 @@ def main(argv=None) -> int:
     ap.add_argument("--e2e-steps", type=int, default=20)
     ap.add_argument("--cpu-seconds", type=float, default=8.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="skip timing the other configurations (run after the timed region, 1 GPU only)")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -15,6 +15,12 @@ int launch_fast(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 // The NVFP4 kernel (t5e_nvfp4.cu); same contract as launch_fast.
 int launch_nvfp4(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 
+// The kind::i8 kernel (t5e_i8.cu); same contract as launch_fast.
+int launch_i8(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
+
+// The TF32/BF16/F16 raw-window kernel (t5e_wide.cu); same contract.
+int launch_wide(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
+
 // Records the last launch error for t5e_last_error(); T5E_OK or T5E_ERR_CUDA.
 int kernel_status(const char* what);
 

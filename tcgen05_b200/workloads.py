@@ -432,3 +432,129 @@ def config_cases(name: str, n: int, seed: int = 0) -> Cases:
         return Cases(dict(a_format="e2m1", scaling="ue4m3", scale_vec=4), a, b, finite_f32_c(rng, n), sa, sb, meta,
                      name=name)
     raise ValueError(f"unknown configuration {name!r}")
+
+
+# ------------------------------------------- configurations generated on the GPU
+
+# Cases per configuration at the sizes the benchmark configurations state.
+CONFIG_SIZES = {
+    "tf32-k8": 65536,
+    "e4m3xe5m2-k32": 1 << 20,
+    "e4m3xe5m2-k32-f16": 1 << 20,
+    "mx-e2m3xe3m2-k32": 1 << 22,
+    "u8xs8-k32-sat": 1 << 22,
+    "u8xs8-k32-wrap": 1 << 22,
+    "nvfp4-k64": 1 << 24,
+    "nvfp4-sparse-k128": 1 << 24,
+    "matrix-bf16": 4096 * 128 * 256,
+}
+
+
+def _device_bytes(torch, gen, device, shape):
+    return torch.randint(0, 256, shape, dtype=torch.uint8, device=device, generator=gen)
+
+
+def _device_finite_c(torch, gen, device, n, f16=False):
+    """Finite C words: F32 with biased exponent uniform in [100, 154] (or F16
+    with exponent in [1, 30]), sign and fraction uniform -- the distribution
+    of finite_f32_c / finite_f16_c."""
+    if f16:
+        sign = torch.randint(0, 2, (n,), dtype=torch.int32, device=device, generator=gen) << 15
+        exp = torch.randint(1, 31, (n,), dtype=torch.int32, device=device, generator=gen) << 10
+        frac = torch.randint(0, 1 << 10, (n,), dtype=torch.int32, device=device, generator=gen)
+        return (sign | exp | frac).to(torch.int16)
+    sign = torch.randint(0, 2, (n,), dtype=torch.int64, device=device, generator=gen) << 31
+    exp = torch.randint(100, 155, (n,), dtype=torch.int64, device=device, generator=gen) << 23
+    frac = torch.randint(0, 1 << 23, (n,), dtype=torch.int64, device=device, generator=gen)
+    return (sign | exp | frac).to(torch.int32)
+
+
+def _device_selector_words(torch, gen, device, n, selectors):
+    sel = torch.as_tensor(selectors.astype(np.int64), device=device)
+    picks = sel[torch.randint(0, len(selectors), (n, 8), device=device, generator=gen)]
+    shifts = torch.arange(8, device=device, dtype=torch.int64) * 4
+    return (picks << shifts).sum(dim=1).to(torch.int64)
+
+
+def device_config(name: str, device, seed: int = 0, n: int | None = None):
+    """A configuration's inputs generated directly in HBM, in the kernels'
+    packed layout, from a seeded device generator: returns (model, DeviceBatch).
+
+    Uniformly random container words of a packed format are uniformly random
+    bytes, so operand rows are random bytes; scales, C and metadata follow
+    the configuration's stated distributions.  (The host generators of
+    config_cases produce the same distributions from numpy; the two streams
+    differ.)"""
+    import torch
+
+    from . import _native as nat
+    from .model import make_model
+    from .runtime import DeviceBatch
+
+    gen = torch.Generator(device=device)
+    gen.manual_seed(seed)
+    n = CONFIG_SIZES[name] if n is None else n
+    if name in ("e4m3xe5m2-k32", "e4m3xe5m2-k32-f16"):
+        f16 = name.endswith("f16")
+        model = make_model("e4m3", "e5m2", d_type="f16" if f16 else "f32")
+        return model, DeviceBatch(n=n, k=32, a=_device_bytes(torch, gen, device, (n, 32)),
+                                  b=_device_bytes(torch, gen, device, (n, 32)),
+                                  c=_device_finite_c(torch, gen, device, n, f16))
+    if name == "tf32-k8":
+        model = make_model("tf32")
+        c = _device_bytes(torch, gen, device, (n, 4)).view(torch.int32).reshape(n)
+        return model, DeviceBatch(n=n, k=8, a=_device_bytes(torch, gen, device, (n, 32)),
+                                  b=_device_bytes(torch, gen, device, (n, 32)), c=c)
+    if name == "mx-e2m3xe3m2-k32":
+        model = make_model("e2m3", "e3m2", scaling="ue8m0", kind="mxf8f6f4")
+        db = DeviceBatch(n=n, k=32, a=_device_bytes(torch, gen, device, (n, 24)),
+                         b=_device_bytes(torch, gen, device, (n, 24)), c=_device_finite_c(torch, gen, device, n))
+        db.scale_a = torch.randint(0x70, 0x90, (n, 1), dtype=torch.uint8, device=device, generator=gen)
+        db.scale_b = torch.randint(0x70, 0x90, (n, 1), dtype=torch.uint8, device=device, generator=gen)
+        return model, db
+    if name in ("u8xs8-k32-sat", "u8xs8-k32-wrap"):
+        model = make_model("u8", "s8", d_type="s32", saturate=name.endswith("sat"))
+        u = torch.randint(0, 1 << 21, (n,), dtype=torch.int64, device=device, generator=gen)
+        top = torch.randint(0, 2, (n,), dtype=torch.int64, device=device, generator=gen).bool()
+        c = torch.where(top, 0x7FFFFFFF - u, 0x80000000 + u).to(torch.int64)
+        c = torch.where(c >= 1 << 31, c - (1 << 32), c).to(torch.int32)
+        return model, DeviceBatch(n=n, k=32, a=_device_bytes(torch, gen, device, (n, 32)),
+                                  b=_device_bytes(torch, gen, device, (n, 32)), c=c)
+    if name in ("nvfp4-k64", "nvfp4-sparse-k128"):
+        model = make_model("e2m1", scaling="ue4m3", scale_vec=4)
+        sparse = name == "nvfp4-sparse-k128"
+        db = DeviceBatch(n=n, k=128 if sparse else 64, a=_device_bytes(torch, gen, device, (n, 32)),
+                         b=_device_bytes(torch, gen, device, (n, 64 if sparse else 32)),
+                         c=_device_finite_c(torch, gen, device, n))
+        db.scale_a = torch.randint(0x01, 0x7F, (n, 4), dtype=torch.uint8, device=device, generator=gen)
+        db.scale_b = torch.randint(0x01, 0x7F, (n, 4), dtype=torch.uint8, device=device, generator=gen)
+        if sparse:
+            lo = _device_selector_words(torch, gen, device, n, SELECTORS_SIX)
+            hi = _device_selector_words(torch, gen, device, n, SELECTORS_SIX)
+            meta = torch.stack([lo, hi], dim=1)
+            db.metadata = torch.where(meta >= 1 << 31, meta - (1 << 32), meta).to(torch.int32)
+            db.sparse = nat.SPARSE_4OF8
+            db.flags = nat.FLAG_SPARSE_A_COMPRESSED
+        return model, db
+    if name == "matrix-bf16":
+        tiles, m, nn = n // (128 * 256), 128, 256
+        model = make_model("bf16")
+        c = _device_bytes(torch, gen, device, (n, 4)).view(torch.int32).reshape(n)
+        return model, DeviceBatch(n=n, k=16, a=_device_bytes(torch, gen, device, (tiles * m, 32)),
+                                  b=_device_bytes(torch, gen, device, (tiles * nn, 32)), c=c, tile_m=m, tile_n=nn)
+    raise ValueError(f"unknown configuration {name!r}")
+
+
+def config_work(name: str, db) -> tuple[int, int]:
+    """(element-MACs, algorithmic bytes) of one launch over DeviceBatch db:
+    physical products per case times cases; bytes of A, B, C, D, scales and
+    metadata the launch must move (matrix tiles read each A and B row once)."""
+    k_phys = 64 if name == "nvfp4-sparse-k128" else db.k
+    macs = db.n * k_phys
+    c_bytes = db.c.element_size()
+    nbytes = db.a.numel() + db.b.numel() + db.n * (c_bytes + 4)
+    if db.scale_a is not None:
+        nbytes += db.scale_a.numel() + db.scale_b.numel()
+    if db.metadata is not None:
+        nbytes += db.metadata.numel() * 4
+    return macs, nbytes

@@ -285,6 +285,33 @@ def test_batched_tiles_match_oracle(desc):
     assert_words_equal(got.reshape(-1), want, str(desc))
 
 
+@pytest.mark.parametrize("desc,k", [(dict(a_format="bf16"), 16), (dict(a_format="tf32"), 8),
+                                    (dict(a_format="f16", d_type="f16"), 16)])
+def test_matrix_configuration_tiles_fast_equals_generic(desc, k):
+    """The matrix configuration's tile shape (M=128, N=256) through the
+    specialised kernel equals the generic kernel, and a sample the oracle."""
+    d = full_desc(desc)
+    rng = np.random.Generator(np.random.PCG64(505))
+    t, m, n = 12, 128, 256
+    fmt = t5.normalize_format(d["a_format"])
+    a = _edge_words(fmt, rng, t * m, k).reshape(t, m, k)
+    bt = _edge_words(fmt, rng, t * n, k).reshape(t, n, k)
+    b = bt.transpose(0, 2, 1).copy()
+    c = (workloads.f16_words(rng, t * m * n) if d["d_type"] == "f16" else workloads.f32_words(rng, t * m * n))
+    c = c.reshape(t, m, n)
+    kw = {kk: d[kk] for kk in KEYS}
+    fast = t5.mma_batch(a, b, c, **kw)
+    generic = t5.mma_batch(a, b, c, generic=True, **kw)
+    assert_words_equal(fast.reshape(-1), generic.reshape(-1), f"{desc} tiles fast vs generic")
+    idx = np.random.Generator(np.random.PCG64(3)).choice(t * m * n, 20000, replace=False)
+    ti, rem = idx // (m * n), idx % (m * n)
+    aa = a[ti, rem // n]
+    bb = bt[ti, rem % n]
+    want, st = oracle.mma_dot_batch(aa, bb, c.reshape(-1)[idx], **kw)
+    assert (st == 0).all()
+    assert_words_equal(fast.reshape(-1)[idx], want, f"{desc} tiles sample vs oracle")
+
+
 def test_matrix_sparse_shares_metadata():
     rng = np.random.Generator(np.random.PCG64(5))
     a = rng.integers(0, 256, size=(8, 64), dtype=np.uint32)

@@ -196,3 +196,42 @@ def test_decoder_handles_for_parameterised_models():
                                       scale_floor_offset=1000, use_c_dominant_merge=False)
     d = m.descriptor()
     assert (d.a_format, d.b_format) == (nat.FMT_E4M3, nat.FMT_E2M1)
+
+
+def test_device_config_generators_follow_the_configurations():
+    """The HBM-side generators (run here on the CPU device) produce the
+    configurations' shapes and value ranges."""
+    import torch
+
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import workloads
+
+    cpu = torch.device("cpu")
+    for name in workloads.CONFIG_SIZES:
+        n = 2 * 128 * 256 if name == "matrix-bf16" else 4096
+        model, db = workloads.device_config(name, cpu, seed=1, n=n)
+        desc = model.descriptor()
+        assert db.n == n
+        from tcgen05_b200 import packing
+        assert db.a.shape[1] >= packing.row_bytes(desc.a_format, 64 if name == "nvfp4-sparse-k128" else db.k)
+        c = db.c.to(torch.int64) & (0xFFFF if db.c.element_size() == 2 else 0xFFFFFFFF)
+        if name.startswith(("e4m3", "mx", "nvfp4")):
+            if db.c.element_size() == 2:
+                e = (c >> 10) & 0x1F
+                assert int(e.min()) >= 1 and int(e.max()) <= 30
+            else:
+                e = (c >> 23) & 0xFF
+                assert int(e.min()) >= 100 and int(e.max()) <= 154
+        if name.startswith("u8xs8"):
+            s = torch.where(c >= 1 << 31, c - (1 << 32), c)
+            assert int(((s > 0) & (s < 0x7FFFFFFF - (1 << 21))).sum()) == 0
+        if db.scale_a is not None:
+            lo, hi = (0x70, 0x8F) if name.startswith("mx") else (0x01, 0x7E)
+            assert int(db.scale_a.min()) >= lo and int(db.scale_a.max()) <= hi
+        if db.metadata is not None:
+            m = db.metadata.to(torch.int64) & 0xFFFFFFFF
+            nib = torch.stack([(m >> (4 * i)) & 0xF for i in range(8)], dim=-1)
+            assert set(nib.unique().tolist()) <= {0x4, 0x8, 0xC, 0x9, 0xD, 0xE}
+            assert db.sparse == nat.SPARSE_4OF8 and db.flags & nat.FLAG_SPARSE_A_COMPRESSED
+        macs, nbytes = workloads.config_work(name, db)
+        assert macs == n * (64 if name.startswith("nvfp4") else db.k)
