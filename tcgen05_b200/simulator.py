@@ -9,6 +9,8 @@ validates arguments, packs operand rows and moves buffers.
 
 from __future__ import annotations
 
+import ctypes
+
 from collections.abc import Sequence
 
 import numpy as np
@@ -425,6 +427,86 @@ def _run(model, a_rows, b_rows, c_dev, k, dev, *, n, tile_m, tile_n, scale_a, sc
     return d
 
 
+def _pinned(x) -> bool:
+    return _is_torch(x) and not x.is_cuda and x.is_pinned()
+
+
+# Batches at least this large, with every per-case array in pinned host
+# memory, are streamed through the GPU in chunks (see _pipelined_batch).
+PIPELINE_MIN_CASES = 1 << 16
+PIPELINE_CHUNKS = 8
+
+
+def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n, dev, out, check, meta_error,
+                     generic):
+    """Host-resident batch in pinned memory -> pinned ``out``: the cases are
+    cut into chunks; each chunk's operands are copied to the device on one
+    stream, evaluated on the current stream once its copy has landed, and its
+    result words (and status bytes) copied back on a third stream, so the
+    copies in both directions overlap each other and the kernels."""
+    import torch
+
+    comp = torch.cuda.current_stream(dev)
+    up = torch.cuda.Stream(dev)
+    down = torch.cuda.Stream(dev)
+    a_dev = torch.empty(a.data.shape, dtype=torch.uint8, device=dev)
+    b_dev = torch.empty(b.data.shape, dtype=torch.uint8, device=dev)
+    c_dev = torch.empty(c.shape, dtype=c.dtype, device=dev)
+    sa_dev = None if sa is None else torch.empty(sa.shape, dtype=torch.uint8, device=dev)
+    sb_dev = None if sb is None else torch.empty(sb.shape, dtype=torch.uint8, device=dev)
+    per_case_meta = meta is not None and not (flags & nat.FLAG_META_BROADCAST)
+    meta_dev = None
+    if meta is not None:
+        meta_dev = (torch.empty(meta.shape, dtype=torch.int32, device=dev) if per_case_meta
+                    else runtime.to_device(meta, dev, torch.int32))
+    d_dev = torch.empty(n, dtype=torch.int32, device=dev)
+    st_dev = torch.empty(n, dtype=torch.uint8, device=dev) if check else None
+    st_host = torch.empty(n, dtype=torch.uint8, pin_memory=True) if check else None
+    lib = nat.load()
+    fn = lib.t5e_mma_dot_batch_generic if generic else lib.t5e_mma_dot_batch
+    handle = ctypes.c_void_p(comp.cuda_stream)
+    step = -(-n // PIPELINE_CHUNKS)
+    step = (step + 1023) // 1024 * 1024
+    sa_h = None if sa is None else sa.view(torch.uint8)
+    sb_h = None if sb is None else sb.view(torch.uint8)
+    for s0 in range(0, n, step):
+        s1 = min(n, s0 + step)
+        with torch.cuda.stream(up):
+            a_dev[s0:s1].copy_(a.data[s0:s1], non_blocking=True)
+            b_dev[s0:s1].copy_(b.data[s0:s1], non_blocking=True)
+            c_dev[s0:s1].copy_(c[s0:s1], non_blocking=True)
+            if sa_dev is not None:
+                sa_dev[s0:s1].copy_(sa_h[s0:s1], non_blocking=True)
+                sb_dev[s0:s1].copy_(sb_h[s0:s1], non_blocking=True)
+            if per_case_meta:
+                meta_dev[s0:s1].copy_(meta[s0:s1].view(torch.int32), non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(up)
+        comp.wait_event(landed)
+        db = runtime.DeviceBatch(n=s1 - s0, k=k, a=a_dev[s0:s1], b=b_dev[s0:s1], c=c_dev[s0:s1], sparse=sparse,
+                                 flags=flags | (nat.FLAG_SPARSE_A_COMPRESSED if a.compressed else 0))
+        if sa_dev is not None:
+            db.scale_a, db.scale_b = sa_dev[s0:s1], sb_dev[s0:s1]
+        if meta_dev is not None:
+            db.metadata = meta_dev[s0:s1] if per_case_meta else meta_dev
+        bs = runtime.make_batch_struct(db, d_dev[s0:s1], None if st_dev is None else st_dev[s0:s1])
+        nat.check(fn(ctypes.byref(desc), ctypes.byref(bs), handle), "t5e_mma_dot_batch")
+        done = torch.cuda.Event()
+        done.record(comp)
+        down.wait_event(done)
+        with torch.cuda.stream(down):
+            out[s0:s1].copy_(d_dev[s0:s1].view(out.dtype), non_blocking=True)
+            if st_dev is not None:
+                st_host[s0:s1].copy_(st_dev[s0:s1], non_blocking=True)
+    down.synchronize()
+    if check:
+        st_np = st_host.numpy()
+        if st_np.any():
+            first = int(np.flatnonzero(st_np)[0])
+            _raise_case_status(selected, int(st_np[first]), meta_message=lambda: meta_error(first))
+    return out
+
+
 def mma_dot_batch(
     a,
     b,
@@ -469,8 +551,15 @@ def mma_dot_batch(
     dev = runtime.require_device(device)
     host_result = not ((_is_torch(a) and a.is_cuda) or (isinstance(a, PackedRows) and _is_torch(a.data)
                                                         and a.data.is_cuda))
-    a_rows, n, ka = _operand_rows(a, desc.a_format, dev, "A")
-    b_rows, nb, k = _operand_rows(b, desc.b_format, dev, "B")
+    streamed = (isinstance(a, PackedRows) and isinstance(b, PackedRows) and _pinned(a.data) and _pinned(b.data)
+                and a.data.dim() == 2 and b.data.dim() == 2)
+    if streamed:  # copied chunk by chunk below, or in one piece if the batch does not qualify
+        a_rows = b_rows = None
+        n, ka = a.data.shape[0], a.k
+        nb, k = b.data.shape[0], b.k
+    else:
+        a_rows, n, ka = _operand_rows(a, desc.a_format, dev, "A")
+        b_rows, nb, k = _operand_rows(b, desc.b_format, dev, "B")
     a_compressed = isinstance(a, PackedRows) and a.compressed
     if nb != n:
         raise ValueError("A and B must hold the same number of cases")
@@ -481,6 +570,27 @@ def mma_dot_batch(
     if k > nat.MAX_K:
         raise ValueError(f"K={k} exceeds the emulator's maximum of {nat.MAX_K}")
     sparse, meta, flags = _prepare(selected, a_format, scaling, kind, k, n, sparse_metadata)
+    if (streamed and out is not None and _pinned(out) and out.element_size() == 4 and n >= PIPELINE_MIN_CASES
+            and c is not None and _pinned(c) and c.element_size() == (2 if desc.d_type == nat.D_F16 else 4)
+            and (scale_a is None or (_pinned(scale_a) and _pinned(scale_b) and scale_a.dim() == 2
+                                     and scale_a.shape == scale_b.shape))
+            and (meta is None or (flags & nat.FLAG_META_BROADCAST) or _pinned(meta))):
+        if scale_a is not None and sparse == 0 and scale_a.shape[1] * desc.scale_block < k:
+            raise ValueError(selected._scale_cover_error)
+
+        def meta_error_p(first: int) -> None:
+            record = meta[0] if meta.shape[0] == 1 else meta[first]
+            words = np.asarray(record.cpu() if _is_torch(record) else record).astype(np.int64).tolist()
+            sparse_active_indices(a_format, k, words[0] if flags & nat.FLAG_META_REPEAT else words,
+                                  kind="nvfp4" if (scaling or "").lower() == "ue4m3" else kind)
+
+        sa_p = scale_a if desc.family in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED) else None
+        sb_p = scale_b if sa_p is not None else None
+        return _pipelined_batch(selected, desc, a, b, c.reshape(n), sa_p, sb_p, meta, flags, sparse, k, n, dev, out,
+                                check, meta_error_p, generic)
+    if streamed:
+        a_rows, _, _ = _operand_rows(a, desc.a_format, dev, "A")
+        b_rows, _, _ = _operand_rows(b, desc.b_format, dev, "B")
     if c is None:
         c_dev = torch.zeros(n, dtype=torch.int16 if desc.d_type == nat.D_F16 else torch.int32, device=dev)
     elif _is_torch(c):

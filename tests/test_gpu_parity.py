@@ -430,3 +430,52 @@ def test_full_size_fast_equals_generic_and_shards(name):
     assert_words_equal(parts, fast, name + " shards")
     sample = np.random.Generator(np.random.PCG64(1)).choice(cases.n, 20000, replace=False)
     assert_words_equal(fast[sample], oracle.eval_cases(cases.subset(sample)), name + " sample vs oracle")
+
+
+@pytest.mark.parametrize("name", ["e4m3xe5m2-k32-f16", "nvfp4-sparse-k128", "u8xs8-k32-wrap"])
+def test_pinned_host_batches_stream_in_chunks(name):
+    """Pinned host operands, C and output take the chunked copy/compute
+    pipeline of mma_dot_batch; its words equal the one-piece evaluation."""
+    import torch
+
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import packing
+
+    n = (1 << 18) + 777  # not a multiple of the chunk size
+    cases = workloads.config_cases(name, n, seed=21)
+    d = full_desc(cases.desc)
+    model = t5.make_model(d["a_format"], d["b_format"], d_type=d["d_type"], saturate=d["saturate"],
+                          scaling=d["scaling"], scale_vec=d["scale_vec"], kind=d["kind"])
+    desc = model.descriptor()
+    a = cases.a
+    compressed = False
+    if cases.meta is not None:
+        act = workloads.active_mask(cases.meta, cases.k, "4of8")
+        a = cases.a[act].reshape(n, -1)
+        compressed = True
+    pa = t5.PackedRows(torch.from_numpy(packing.pack_rows(a, desc.a_format)).pin_memory(), a.shape[1], compressed)
+    pb = t5.PackedRows(torch.from_numpy(packing.pack_rows(cases.b, desc.b_format)).pin_memory(), cases.k)
+    f16 = desc.d_type == nat.D_F16
+    c = torch.from_numpy((cases.c & 0xFFFF).astype(np.uint16).view(np.int16) if f16 else cases.c.view(np.int32))
+    kw = {}
+    if cases.scale_a is not None:
+        kw["scale_a"] = torch.from_numpy(cases.scale_a).pin_memory()
+        kw["scale_b"] = torch.from_numpy(cases.scale_b).pin_memory()
+    if cases.meta is not None:
+        kw["sparse_metadata"] = torch.from_numpy(cases.meta.view(np.int32)).pin_memory()
+    out = torch.empty(n, dtype=torch.int32).pin_memory()
+    # the sparse geometry comes from the keywords, as in the reference's mma_dot
+    kw.update({kk: d[kk] for kk in KEYS})
+    got = t5.mma_dot_batch(pa, pb, c.pin_memory(), out=out, **kw)
+    assert got is out
+    want = gpu_cases(cases)
+    assert_words_equal(out.numpy().view(np.uint32), want, name + " streamed vs one piece")
+    sample = np.random.Generator(np.random.PCG64(2)).choice(n, 4096, replace=False)
+    assert_words_equal(out.numpy().view(np.uint32)[sample], oracle.eval_cases(cases.subset(sample)),
+                       name + " streamed sample vs oracle")
+    if cases.meta is not None:
+        bad = cases.meta.copy()
+        bad[n - 5, 1] = (bad[n - 5, 1] & ~np.uint32(0xF)) | np.uint32(0x3)  # illegal selector in the last chunk
+        kw["sparse_metadata"] = torch.from_numpy(bad.view(np.int32)).pin_memory()
+        with pytest.raises(ValueError):
+            t5.mma_dot_batch(pa, pb, c.pin_memory(), out=out, **kw)

@@ -1,0 +1,141 @@
+"""The 46-path sweep driver: its counter-hash case generator (numpy and torch
+produce the same words), the distributions it draws, its sharding and
+cross-rank reduction (world size 2 over gloo on the CPU), its integrity
+checks, and -- on a GPU -- every path against the oracle."""
+
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from tcgen05_b200 import sweep, workloads
+
+PATHS = workloads.validation_paths()
+
+
+@pytest.mark.parametrize("spec", PATHS, ids=lambda s: s.name)
+def test_generator_numpy_and_torch_agree(spec):
+    total = 1000
+    g_np = sweep.generate(spec, 480, 40, total, np)  # straddles the raw/finite halves
+    g_t = sweep.generate(spec, 480, 40, total, torch, torch.device("cpu"))
+    for key, v in g_np.items():
+        if v is None:
+            assert g_t[key] is None
+            continue
+        assert np.array_equal(np.asarray(v, dtype=np.int64), g_t[key].numpy().astype(np.int64)), key
+
+
+@pytest.mark.parametrize("spec", PATHS, ids=lambda s: s.name)
+def test_generated_cases_are_valid_inputs(spec):
+    """Words fit their containers, finite halves hold no specials, and the
+    oracle accepts every case (legal metadata, matching scale counts)."""
+    from oracle import oracle
+
+    total = 512
+    cases = sweep.host_cases(spec, 0, total, total)
+    assert cases.k == sweep.path_k(spec)
+    _, st = oracle.mma_dot_batch(cases.a, cases.b, cases.c, scale_a=cases.scale_a, scale_b=cases.scale_b,
+                                 sparse_metadata=cases.meta, **{k: v for k, v in spec.descriptor.items()})
+    assert (st == 0).all()
+    d = spec.descriptor
+    fin = cases.a[total // 2:]
+    if spec.family == "dense" and d["a_format"] in ("tf32", "bf16"):
+        assert not ((fin & 0x7F800000) == 0x7F800000).any()
+        assert ((cases.a[: total // 2] & 0x7F800000) == 0x7F800000).any()
+    if spec.family == "dense" and d["a_format"] == "e4m3":
+        assert not ((fin & 0x7F) == 0x7F).any()
+    if spec.family == "i8":
+        assert cases.a[0].tolist() == [0] * 32 and cases.c[3] == 0x7FFFFFF0
+
+
+def test_generator_is_shard_independent():
+    spec = next(p for p in PATHS if p.name == "sparse-nvfp4")
+    whole = sweep.host_cases(spec, 0, 300, 300)
+    parts = sweep.host_cases(spec, 0, 100, 300).concat(sweep.host_cases(spec, 100, 200, 300))
+    assert whole.digest() == parts.digest()
+
+
+def _fake_evaluate(spec, lo, hi, total):
+    """A device-free stand-in for the GPU evaluation: folds the generated C
+    words (a deterministic function of the case index) into the checksum."""
+    g = sweep.generate(spec, lo, hi - lo, total, np)
+    idx = np.arange(lo, hi, dtype=np.int64)
+    return hi - lo, 0, sweep.result_checksum(np, idx, np.asarray(g["c"], dtype=np.int64))
+
+
+def _worker(rank, world, port, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rep = sweep.run_sweep(777, paths=PATHS[:6], rank=rank, world=world, evaluate=_fake_evaluate)
+        q.put((rank, [(r["path"], r["cases"], r["checksum"]) for r in rep["results"]], rep["failed_paths"]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_over_gloo_match_one_rank():
+    import multiprocessing as mp
+
+    single = sweep.run_sweep(777, paths=PATHS[:6], evaluate=_fake_evaluate)
+    want = [(r["path"], r["cases"], r["checksum"]) for r in single["results"]]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29000 + os.getpid() % 1000
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = [q.get(timeout=120) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, rows, failed in got:
+        assert rows == want, rank
+        assert failed == []
+
+
+def test_shards_cover_every_case_once():
+    for total in (1, 7, 1000, 1_000_000):
+        for world in (1, 2, 3, 4, 8):
+            bounds = [sweep.shard(total, r, world) for r in range(world)]
+            assert bounds[0][0] == 0 and bounds[-1][1] == total
+            assert all(bounds[i][1] == bounds[i + 1][0] for i in range(world - 1))
+
+
+def test_integrity_checks():
+    req = ["a", "b", "c"]
+    ok = [{"path": p, "failed": False} for p in req]
+    assert sweep.integrity(req, ok) == ([], [])
+    bad = [{"path": "a", "failed": False}, {"path": "a", "failed": False}, {"path": "x", "failed": True}]
+    failed, errors = sweep.integrity(req, bad)
+    assert failed == ["b", "c", "x"]
+    assert errors == ["missing paths: b, c", "duplicate paths: a", "unexpected paths: x"]
+
+
+@pytest.mark.gpu
+def test_gpu_sweep_every_path_matches_generic_and_oracle():
+    from oracle import oracle
+
+    dev = torch.device("cuda", 0)
+    total = 8192
+    rep = sweep.run_sweep(total, device=dev, chunk=3000)
+    assert rep["failed_paths"] == [] and rep["integrity_errors"] == []
+    assert all(r["mismatches"] == 0 and r["cases"] == total for r in rep["results"])
+    for spec in PATHS:
+        lo, hi = 4000, 4300  # straddles the raw/finite halves
+        g = sweep.generate(spec, lo, hi - lo, total, torch, dev)
+        got = sweep._device_eval(spec, g, dev, generic=False).cpu().numpy().astype(np.uint32)
+        want = oracle.eval_cases(sweep.host_cases(spec, lo, hi - lo, total))
+        assert np.array_equal(got, want), spec.name
+    # the same report from two shards evaluated separately
+    halves = [sweep.run_sweep(total, rank=r, world=1, device=dev, paths=PATHS[:4],
+                              evaluate=lambda s, lo, hi, t, r=r: sweep._evaluate_shard_gpu(
+                                  s, *sweep.shard(t, r, 2), t, dev, 4096)) for r in range(2)]
+    whole = sweep.run_sweep(total, device=dev, paths=PATHS[:4])
+    for i in range(4):
+        s = (int(halves[0]["results"][i]["checksum"], 16) + int(halves[1]["results"][i]["checksum"], 16))
+        assert s == int(whole["results"][i]["checksum"], 16)
