@@ -343,57 +343,19 @@ OTHER_CONFIGS = ("tf32-k8", "mx-e2m3xe3m2-k32", "u8xs8-k32-sat", "u8xs8-k32-wrap
 
 def measure_configs(torch, device, lib, launches: int = 20, warmup: int = 3) -> dict:
     """Every other benchmark configuration at its stated size, generated in
-    HBM: mean CUDA-event time of one launch of t5e_mma_dot_batch (L2 flushed
-    before each timed launch by writing a 256 MB buffer), element-MACs/s,
-    algorithmic GB/s and its fraction of the measured HBM peak, and the
-    number of result words that differ from the generic kernel on the first
-    2^18 cases."""
-    from tcgen05_b200 import _native as nat
-    from tcgen05_b200 import runtime, workloads
+    HBM (tcgen05_b200.launch_config.time_config): mean CUDA-event time of one
+    launch of t5e_mma_dot_batch with the L2 flushed before each timed launch,
+    element-MACs/s, algorithmic GB/s and its fraction of the measured HBM
+    peak, and the number of result words that differ from the generic kernel
+    on the first 2^18 cases."""
+    from tcgen05_b200.launch_config import time_config
 
     peaks, _ = measured_peaks()
-    stream = torch.cuda.current_stream(device)
-    handle = ctypes.c_void_p(stream.cuda_stream)
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     out = {}
     for idx, name in enumerate(OTHER_CONFIGS):
-        model, db = workloads.device_config(name, device, seed=1000 + idx)
-        desc = model.descriptor()
-        d = torch.empty(db.n, dtype=torch.int32, device=device)
-        bs = runtime.make_batch_struct(db, d, None)
-
-        def run(fn, s=bs):
-            rc = fn(ctypes.byref(desc), ctypes.byref(s), handle)
-            nat.check(rc, name)
-
-        for _ in range(warmup):
-            run(lib.t5e_mma_dot_batch)
-        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(launches)]
-        for e0, e1 in ev:
-            flush.zero_()
-            e0.record(stream)
-            run(lib.t5e_mma_dot_batch)
-            e1.record(stream)
-        torch.cuda.synchronize(device)
-        us = statistics.mean(e0.elapsed_time(e1) for e0, e1 in ev) * 1e3
-        # parity on a prefix: the dispatching entry point vs the generic kernel
-        per = db.tile_m * db.tile_n
-        m = min(db.n, max(per, (1 << 18) // per * per))
-        sub = runtime.make_batch_struct(db, d, None)
-        sub.n = m
-        gen = torch.empty(m, dtype=torch.int32, device=device)
-        sub_g = runtime.make_batch_struct(db, gen, None)
-        sub_g.n = m
-        run(lib.t5e_mma_dot_batch, sub)
-        run(lib.t5e_mma_dot_batch_generic, sub_g)
-        torch.cuda.synchronize(device)
-        mism = int((d[:m] != gen).sum().item())
-        macs, nbytes = workloads.config_work(name, db)
-        gbs = nbytes / (us * 1e-6) / 1e9
-        out[name] = {"cases": db.n, "k": db.k, "kernel_us": us, "value": macs / (us * 1e-6),
-                     "dot_products_per_s": db.n / (us * 1e-6), "algorithmic_gbs": gbs,
-                     "hbm_frac": gbs / peaks["hbm_gbs"], "mismatches_vs_generic": mism, "checked_cases": m}
-        del db, d, gen, bs, sub, sub_g
+        r = time_config(name, device, launches=launches, warmup=warmup, seed=1000 + idx)
+        r["hbm_frac"] = r["algorithmic_gbs"] / peaks["hbm_gbs"]
+        out[name] = r
         torch.cuda.empty_cache()
     return out
 

@@ -154,8 +154,9 @@ __global__ void __launch_bounds__(kThreads) wide_kernel(const t5e_batch B, int f
 // tile's A rows are decoded once into shared memory as (signed significand,
 // raw exponent) pairs; each thread keeps one B column decoded in registers
 // (significands pre-shifted by S0) and walks the rows, reading each A row
-// by broadcast.  A row or column holding NaN or Inf sends its cases through
-// eval_rows on the packed words.
+// by broadcast.  A NaN in a case's A row or B column makes its result NaN;
+// a row or column holding infinities and no NaN sends its cases through
+// eval_rows on the packed words in a second sweep.
 constexpr int kTileRowsMax = 256;
 constexpr int kTileColsMax = 4096;
 
@@ -176,6 +177,8 @@ __global__ void __launch_bounds__(kThreads) wide_tile_kernel(const t5e_batch B, 
   const uint32_t tiles = (uint32_t)(B.n / ((uint64_t)tm * (uint64_t)tn));
   for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
     __syncthreads();  // the previous tile's rows are no longer read
+    for (int row = threadIdx.x; row < tm; row += blockDim.x) aspecial[row] = 0;
+    __syncthreads();
     for (int e = threadIdx.x; e < tm * K; e += blockDim.x) {
       const int row = e / K, k = e - row * K;
       const uint32_t* w = reinterpret_cast<const uint32_t*>(Abase + ((size_t)t * tm + row) * 32);
@@ -184,33 +187,40 @@ __global__ void __launch_bounds__(kThreads) wide_tile_kernel(const t5e_batch B, 
       const bool sp = a.nan | a.inf;
       am[e] = sp ? 0 : a.m;
       ar[e] = sp ? -kBig : a.re;
-      if (k == 0) aspecial[row] = 0;
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < tm * K; e += blockDim.x) {
-      if (ar[e] == -kBig) aspecial[e / K] = 1;  // benign race: every writer stores 1
+      if (sp) atomicOr(&aspecial[row], a.nan ? 1 : 2);  // bit 0: a NaN, bit 1: an infinity
     }
     __syncthreads();
     for (int j = threadIdx.x; j < tn; j += blockDim.x) {
       uint32_t wb[8];
       load32(Bbase + ((size_t)t * tn + j) * 32, wb);
       int32_t bm[K], br[K];
-      bool bspecial = false;
+      bool bnan = false, binf = false;
 #pragma unroll
       for (int k = 0; k < K; ++k) {
         const Elem<F> b = decode<F>(T::elem(wb, k));
-        bspecial |= b.nan | b.inf;
+        bnan |= b.nan;
+        binf |= b.inf;
         bm[k] = b.m * (1 << S0);
         br[k] = b.re;
       }
-      bflag[j] = bspecial;
-      if (bspecial) continue;  // second sweep
+      bflag[j] = (bnan ? 1 : 0) | (binf ? 2 : 0);
       const size_t case0 = (size_t)t * tm * tn + j;
-      for (int i = 0; i < tm; ++i) {
-        if (aspecial[i]) continue;  // second sweep
+      auto c_at = [&](int i) {
         const size_t ci = case0 + (size_t)i * tn;
-        const uint32_t cword = F16D ? (uint32_t)__ldg(static_cast<const uint16_t*>(B.c) + ci)
-                                    : __ldg(static_cast<const uint32_t*>(B.c) + ci);
+        return F16D ? (uint32_t)__ldg(static_cast<const uint16_t*>(B.c) + ci) : __ldg(static_cast<const uint32_t*>(B.c) + ci);
+      };
+      uint32_t c_next = c_at(0);  // C of the next row is in flight while this row is evaluated
+      for (int i = 0; i < tm; ++i) {
+        const uint32_t cword = c_next;
+        if (i + 1 < tm) c_next = c_at(i + 1);
+        const int af = aspecial[i];
+        const size_t ci = case0 + (size_t)i * tn;
+        if (bnan || (af & 1)) {  // a NaN element makes a NaN product (model.py:391-392)
+          B.d[ci] = 0x7FFFFFFFu;
+          if (B.status) B.status[ci] = (uint8_t)T5E_CASE_OK;
+          continue;
+        }
+        if (af || binf) continue;  // infinities and no NaN: second sweep
         const int32_t* arow_m = am + i * K;
         const int32_t* arow_r = ar + i * K;
         int32_t pm[K], pr[K];
@@ -251,14 +261,17 @@ __global__ void __launch_bounds__(kThreads) wide_tile_kernel(const t5e_batch B, 
         if (B.status) B.status[ci] = (uint8_t)T5E_CASE_OK;
       }
     }
-    // second sweep: cases whose A row or B column holds NaN or Inf
+    // second sweep: cases with an infinity and no NaN in their A row and B
+    // column (the others are done)
     for (int j = threadIdx.x; j < tn; j += blockDim.x) {
-      const bool bspecial = bflag[j] != 0;
+      const int bf = bflag[j];
+      if (bf & 1) continue;
       uint32_t wb[8];
       bool loaded = false;
       const size_t case0 = (size_t)t * tm * tn + j;
       for (int i = 0; i < tm; ++i) {
-        if (!bspecial && !aspecial[i]) continue;
+        const int af = aspecial[i];
+        if ((af & 1) || !(bf | af)) continue;
         if (!loaded) {
           load32(Bbase + ((size_t)t * tn + j) * 32, wb);
           loaded = true;
