@@ -2,7 +2,7 @@
 tcgen05_model arithmetic (oracle/t5e_oracle.c).
 
 Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-bench.py use this module, as the parity checker and the timed CPU baseline.
+bench.py use this module, as the parity reference and the timed CPU baseline.
 The product path (tcgen05_b200) never imports it.
 
 ``mma_dot_batch`` takes the public ``mma_dot`` arguments for N cases

@@ -2,7 +2,7 @@
  * t5e_oracle.c -- TEST INFRASTRUCTURE ONLY.
  *
  * A plain-C, single-case-at-a-time restatement of the tcgen05_model arithmetic
- * (the reference Python package sf-tensor/tcgen05).  It is the parity checker
+ * (the reference Python package sf-tensor/tcgen05).  It is the parity reference
  * for the CUDA emulator and the timed CPU baseline ("port") in bench.py.  It is
  * never linked into, called by, or shipped with the product path.
  *

@@ -1,6 +1,6 @@
 """Pin the CPU oracle (oracle/t5e_oracle.c) to the reference.
 
-The oracle is the parity checker of the CUDA emulator, so before any GPU
+The oracle is the parity reference of the CUDA emulator, so before any GPU
 result is compared with it, it must reproduce the reference exactly:
 
 * the frozen B200 words of tcgen05_model/validation.py:37-344 and the
