@@ -156,7 +156,7 @@ typedef struct t5e_batch {
 #define T5E_CASE_SCALE_COVER 3    /* more K than scale blocks cover, model.py:730-731, 857-858 */
 #define T5E_CASE_META_WORDS 4     /* too few metadata nibbles, simulator.py:60-61 */
 #define T5E_CASE_TIMEOUT 5        /* reserved for kernels with bounded device waits (no result word);
-                                     no kernel of this library waits, so none sets it today */
+                                     no emulator kernel waits, so none sets it today */
 
 /* library ABI version (T5E_ABI_VERSION) */
 int t5e_abi_version(void);
@@ -183,6 +183,21 @@ int t5e_pack_rows(int32_t format, const uint32_t* words, uint64_t rows, int32_t 
  * active[0..k) receives 0/1; returns T5E_CASE_* (0 when legal). */
 int t5e_sparse_active(int32_t sparse, int32_t k, const uint32_t* words, int32_t nwords,
                       int32_t repeat, uint8_t* active);
+
+/* Hardware cross-check (no counterpart in the reference's model package; it
+ * plays the part of the reference harness's probe runners,
+ * hardware_validation/src/tcgen05_*_probe.cu).  Issues real tcgen05.mma
+ * instructions: for each of `tiles` tiles, D = A B + C with M = 128, N = 16
+ * and one instruction's K, all operands 32-byte K-major rows:
+ *   a: tiles*128 rows, b: tiles*16 rows (the columns of B), c, d: tiles*128*16
+ *   32-bit words (row-major), F32 or S32 accumulators only.
+ * `idesc` is the tcgen05 instruction descriptor (formats, M, N, saturation)
+ * and `kind` the instruction kind.  *error (a device word, initialised to 0
+ * by the caller) becomes 1 if a product did not complete within the kernel's
+ * bounded wait; the affected tiles are then left unwritten. */
+enum { T5E_HW_TF32 = 0, T5E_HW_F16 = 1, T5E_HW_F8F6F4 = 2, T5E_HW_I8 = 3 };
+int t5e_tcgen05_tiles(int32_t kind, uint32_t idesc, const void* a, const void* b, const uint32_t* c, uint32_t* d,
+                      uint64_t tiles, int32_t* error, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,200 @@
+// t5e_tcgen05.cu -- the hardware side of the cross-check: real tcgen05.mma
+// instructions on the B200's tensor cores, for comparing the emulator's words
+// with the hardware's (the role of the reference harness's probe runners,
+// hardware_validation/src/tcgen05_*_probe.cu, written anew).
+//
+// One CTA of 128 threads per tile D = A B + C with M = 128, N = 16 and one
+// instruction's K (8 TF32, 16 F16/BF16, 32 FP8 or 8-bit integers: 32-byte
+// K-major rows in every case):
+//
+//  * A (128 rows) and B (16 rows) are staged in shared memory in the
+//    non-swizzled K-major layout: 8-row x 16-byte core matrices, the two
+//    16-byte halves of a row 128 bytes apart (leading byte offset) and groups
+//    of 8 rows 256 bytes apart (stride byte offset);
+//  * C is written into tensor memory (TMEM lane = row, column = n) with
+//    tcgen05.st, one tcgen05.mma.cta_group::1 accumulates onto it, and
+//    tcgen05.commit arrives on an mbarrier when the product is complete;
+//  * every thread waits on that mbarrier with a bounded number of polls; a
+//    wait that runs out sets the error word and the CTA stops (freeing its
+//    tensor memory) instead of hanging;
+//  * each thread reads its row of D back with tcgen05.ld.
+//
+// Only F32 and S32 accumulators are handled (one 32-bit TMEM column per n).
+// No TMA, no clusters, no multicast.
+#include <cuda_runtime.h>
+
+#include "t5e.h"
+#include "t5e_dispatch.h"
+
+namespace t5e {
+namespace hw {
+
+constexpr int kRows = 128, kCols = 16, kRowBytes = 32, kTmemCols = 32;
+constexpr uint32_t kWaitPolls = 1u << 20;  // bounded mbarrier polls per tile
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Shared-memory matrix descriptor: start address, leading byte offset 128,
+// stride byte offset 256 (all in 16-byte units), descriptor version 1, no
+// swizzle.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(128 >> 4) << 16) | ((uint64_t)(256 >> 4) << 32) |
+         (1ull << 46);
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc) {
+  const uint32_t zero = 0, accumulate = 1;
+  if constexpr (KIND == T5E_HW_TF32) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(zero));
+  } else if constexpr (KIND == T5E_HW_F16) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(zero));
+  } else if constexpr (KIND == T5E_HW_F8F6F4) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(zero));
+  } else {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(zero));
+  }
+}
+
+__device__ __forceinline__ bool wait_phase(uint32_t mbar, uint32_t phase) {
+  for (uint32_t poll = 0; poll < kWaitPolls; ++poll) {
+    uint32_t done;
+    asm volatile("{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+                 "selp.b32 %0, 1, 0, P1;\n\t}\n"
+                 : "=r"(done) : "r"(mbar), "r"(phase) : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kRows) tcgen05_tile_kernel(const uint8_t* __restrict__ A, const uint8_t* __restrict__ B,
+                                                             const uint32_t* __restrict__ C, uint32_t* __restrict__ D,
+                                                             uint32_t idesc, uint32_t tiles, int* error) {
+  __shared__ __align__(128) uint8_t sA[kRows * kRowBytes];
+  __shared__ __align__(128) uint8_t sB[kCols * kRowBytes];
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ uint32_t tmem_slot;
+  const int t = threadIdx.x, warp = t >> 5;
+  const uint32_t bar = smem_u32(&mbar);
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(&tmem_slot)), "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (t == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(1));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  uint32_t phase = 0;
+  for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    // stage row t of A and, for t < 16, row t of B in the core-matrix layout
+    const uint4* ga = reinterpret_cast<const uint4*>(A + ((size_t)tile * kRows + t) * kRowBytes);
+    const uint4 a0 = __ldg(ga), a1 = __ldg(ga + 1);
+    *reinterpret_cast<uint4*>(sA + (t >> 3) * 256 + (t & 7) * 16) = a0;
+    *reinterpret_cast<uint4*>(sA + (t >> 3) * 256 + 128 + (t & 7) * 16) = a1;
+    if (t < kCols) {
+      const uint4* gb = reinterpret_cast<const uint4*>(B + ((size_t)tile * kCols + t) * kRowBytes);
+      const uint4 b0 = __ldg(gb), b1 = __ldg(gb + 1);
+      *reinterpret_cast<uint4*>(sB + (t >> 3) * 256 + (t & 7) * 16) = b0;
+      *reinterpret_cast<uint4*>(sB + (t >> 3) * 256 + 128 + (t & 7) * 16) = b1;
+    }
+    // C row t into TMEM lane t, columns 0..15
+    const uint32_t* crow = C + ((size_t)tile * kRows + t) * kCols;
+    uint32_t c[kCols];
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) c[j] = __ldg(crow + j);
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                 "%13, %14, %15, %16};"
+                 :: "r"(lane_base), "r"(c[0]), "r"(c[1]), "r"(c[2]), "r"(c[3]), "r"(c[4]), "r"(c[5]), "r"(c[6]),
+                    "r"(c[7]), "r"(c[8]), "r"(c[9]), "r"(c[10]), "r"(c[11]), "r"(c[12]), "r"(c[13]), "r"(c[14]),
+                    "r"(c[15]) : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // smem operands visible to the tensor core
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (t == 0) {
+      mma<KIND>(tmem, smem_desc(smem_u32(sA)), smem_desc(smem_u32(sB)), idesc);
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                   :: "r"(bar) : "memory");
+    }
+    const bool ok = wait_phase(bar, phase);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) {  // the product never arrived: record it and stop
+      if (t == 0) atomicExch(error, 1);
+      break;
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    uint32_t d[kCols];
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, "
+                 "%13, %14, %15}, [%16];"
+                 : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3]), "=r"(d[4]), "=r"(d[5]), "=r"(d[6]), "=r"(d[7]),
+                   "=r"(d[8]), "=r"(d[9]), "=r"(d[10]), "=r"(d[11]), "=r"(d[12]), "=r"(d[13]), "=r"(d[14]), "=r"(d[15])
+                 : "r"(lane_base) : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+    uint32_t* drow = D + ((size_t)tile * kRows + t) * kCols;
+#pragma unroll
+    for (int j = 0; j < kCols; ++j) drow[j] = d[j];
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();  // shared memory and TMEM are reused by the next tile
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(kTmemCols));
+  }
+}
+
+template <int KIND>
+int launch(const void* a, const void* b, const uint32_t* c, uint32_t* d, uint64_t tiles, uint32_t idesc, int* error,
+           cudaStream_t stream) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t cap = (uint64_t)sms * 4u;
+  const int grid = (int)(tiles < cap ? tiles : cap);
+  tcgen05_tile_kernel<KIND><<<grid, kRows, 0, stream>>>(static_cast<const uint8_t*>(a), static_cast<const uint8_t*>(b),
+                                                        c, d, idesc, (uint32_t)tiles, error);
+  return kernel_status("tcgen05_tile_kernel launch");
+}
+
+}  // namespace hw
+}  // namespace t5e
+
+extern "C" int t5e_tcgen05_tiles(int32_t kind, uint32_t idesc, const void* a, const void* b, const uint32_t* c,
+                                 uint32_t* d, uint64_t tiles, int32_t* error, void* stream) {
+  using namespace t5e::hw;
+  if (tiles == 0) return T5E_OK;
+  if (!a || !b || !c || !d || !error || tiles >= (1ull << 31)) return T5E_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) % 16 != 0) return T5E_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d)) % 4 != 0) return T5E_ERR_INVALID;
+  // the descriptor must describe M=128, N=16, both operands K-major, dense, with
+  // an F32 or S32 accumulator
+  if (((idesc >> 24) & 0x1Fu) != 8u || ((idesc >> 17) & 0x3Fu) != 2u) return T5E_ERR_INVALID;
+  if ((idesc & 0x7u) != 0u || ((idesc >> 15) & 3u) != 0u) return T5E_ERR_INVALID;
+  const uint32_t cfmt = (idesc >> 4) & 3u;
+  if (cfmt != 1u && cfmt != 2u) return T5E_ERR_UNSUPPORTED;
+  int* err = reinterpret_cast<int*>(error);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (kind) {
+    case T5E_HW_TF32: return launch<T5E_HW_TF32>(a, b, c, d, tiles, idesc, err, s);
+    case T5E_HW_F16: return launch<T5E_HW_F16>(a, b, c, d, tiles, idesc, err, s);
+    case T5E_HW_F8F6F4: return launch<T5E_HW_F8F6F4>(a, b, c, d, tiles, idesc, err, s);
+    case T5E_HW_I8: return launch<T5E_HW_I8>(a, b, c, d, tiles, idesc, err, s);
+    default: return T5E_ERR_INVALID;
+  }
+}
