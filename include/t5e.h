@@ -190,9 +190,13 @@ int t5e_sparse_active(int32_t sparse, int32_t k, const uint32_t* words, int32_t 
  * instructions: for each of `tiles` tiles, D = A B + C with M = 128, N = 16
  * and one instruction's K, all operands 32-byte K-major rows:
  *   a: tiles*128 rows, b: tiles*16 rows (the columns of B), c, d: tiles*128*16
- *   32-bit words (row-major), F32 or S32 accumulators only.
+ *   32-bit words (row-major): F32, S32, or F16 in the low 16 bits.
+ * A row of E2M3/E3M2/E2M1 elements (kind::f8f6f4) is two 16-byte chunks, each
+ * holding 16 packed elements followed by zero padding.
  * `idesc` is the tcgen05 instruction descriptor (formats, M, N, saturation)
- * and `kind` the instruction kind.  *error (a device word, initialised to 0
+ * and `kind` the instruction kind; descriptors outside the documented
+ * encodings for M = 128, N = 16, dense K-major operands are rejected
+ * (T5E_ERR_INVALID) before anything is launched.  *error (a device word, initialised to 0
  * by the caller) becomes 1 if a product did not complete within the kernel's
  * bounded wait; the affected tiles are then left unwritten. */
 enum { T5E_HW_TF32 = 0, T5E_HW_F16 = 1, T5E_HW_F8F6F4 = 2, T5E_HW_I8 = 3 };

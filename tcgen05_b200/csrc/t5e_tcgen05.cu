@@ -19,8 +19,11 @@
 //    tensor memory) instead of hanging;
 //  * each thread reads its row of D back with tcgen05.ld.
 //
-// Only F32 and S32 accumulators are handled (one 32-bit TMEM column per n).
-// No TMA, no clusters, no multicast.
+// Accumulators take one 32-bit TMEM column per n: F32, S32, or F16 in the low
+// half of the column.  FP6 and FP4 operands of kind::f8f6f4 sit in shared
+// memory as 16-byte chunks of 16 packed elements followed by zero padding, so
+// their 32-element rows are 32 bytes like the 8-bit ones.  No TMA, no
+// clusters, no multicast.
 #include <cuda_runtime.h>
 
 #include "t5e.h"
@@ -159,6 +162,28 @@ __global__ void __launch_bounds__(kRows) tcgen05_tile_kernel(const uint8_t* __re
   }
 }
 
+// The instruction descriptors this kernel's layouts implement, and only
+// documented encodings of them: dense, A and B K-major, no negation or shift,
+// M = 128, N = 16; per kind the operand format codes the instruction defines
+// (kind::f16 with one type for A and B), the accumulator format (F16 only for
+// F16 x F16 or f8f6f4 operands) and saturation for kind::i8 only.
+bool descriptor_ok(int32_t kind, uint32_t idesc) {
+  const uint32_t fields = (1u << 3) | (3u << 4) | (7u << 7) | (7u << 10) | (0x3Fu << 17) | (0x1Fu << 24);
+  if ((idesc & ~fields) != 0u) return false;
+  if (((idesc >> 24) & 0x1Fu) != 8u || ((idesc >> 17) & 0x3Fu) != 2u) return false;
+  const uint32_t sat = (idesc >> 3) & 1u, cfmt = (idesc >> 4) & 3u;
+  const uint32_t af = (idesc >> 7) & 7u, bf = (idesc >> 10) & 7u;
+  constexpr uint32_t kF16 = 0u, kF32 = 1u, kS32 = 2u;
+  auto f8f6f4 = [](uint32_t f) { return f == 0u || f == 1u || f == 3u || f == 4u || f == 5u; };
+  switch (kind) {
+    case T5E_HW_TF32: return af == 2u && bf == 2u && cfmt == kF32 && !sat;
+    case T5E_HW_F16: return af <= 1u && bf == af && (cfmt == kF32 || (cfmt == kF16 && af == 0u)) && !sat;
+    case T5E_HW_F8F6F4: return f8f6f4(af) && f8f6f4(bf) && (cfmt == kF32 || cfmt == kF16) && !sat;
+    case T5E_HW_I8: return af <= 1u && bf <= 1u && cfmt == kS32;
+    default: return false;
+  }
+}
+
 template <int KIND>
 int launch(const void* a, const void* b, const uint32_t* c, uint32_t* d, uint64_t tiles, uint32_t idesc, int* error,
            cudaStream_t stream) {
@@ -182,12 +207,7 @@ extern "C" int t5e_tcgen05_tiles(int32_t kind, uint32_t idesc, const void* a, co
   if (!a || !b || !c || !d || !error || tiles >= (1ull << 31)) return T5E_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) % 16 != 0) return T5E_ERR_INVALID;
   if ((reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d)) % 4 != 0) return T5E_ERR_INVALID;
-  // the descriptor must describe M=128, N=16, both operands K-major, dense, with
-  // an F32 or S32 accumulator
-  if (((idesc >> 24) & 0x1Fu) != 8u || ((idesc >> 17) & 0x3Fu) != 2u) return T5E_ERR_INVALID;
-  if ((idesc & 0x7u) != 0u || ((idesc >> 15) & 3u) != 0u) return T5E_ERR_INVALID;
-  const uint32_t cfmt = (idesc >> 4) & 3u;
-  if (cfmt != 1u && cfmt != 2u) return T5E_ERR_UNSUPPORTED;
+  if (!descriptor_ok(kind, idesc)) return T5E_ERR_INVALID;
   int* err = reinterpret_cast<int*>(error);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (kind) {

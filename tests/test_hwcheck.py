@@ -1,11 +1,14 @@
 """The hardware cross-check: its tcgen05 instruction descriptors equal the
 ones CUTLASS's own descriptor code builds (compiled here for the host from
-the CUTLASS headers in the image), its arguments are validated, and -- on a
-B200 -- real tcgen05.mma words equal the emulator's for every kind it
-issues."""
+the CUTLASS headers in the image), the C ABI rejects every descriptor
+outside the documented encodings before launching anything, the sub-byte
+operand rows have the f8f6f4 shared-memory form, and -- on a B200 -- real
+tcgen05.mma words equal the emulator's for every kind, operand pair and
+accumulator it issues."""
 
 from __future__ import annotations
 
+import ctypes
 import os
 import shutil
 import subprocess
@@ -14,6 +17,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+from tcgen05_b200 import _native as nat
 from tcgen05_b200 import hwcheck
 
 
@@ -26,13 +30,22 @@ def _cutlass_include():
     return p if (p / "cute" / "arch" / "mma_sm100_desc.hpp").exists() else None
 
 
-CASES = [("tf32", "tf32", False, "tfloat32_t", "tfloat32_t", "float"),
-         ("bf16", "bf16", False, "bfloat16_t", "bfloat16_t", "float"),
-         ("f16", "f16", False, "half_t", "half_t", "float"),
-         ("e4m3", "e5m2", False, "float_e4m3_t", "float_e5m2_t", "float"),
-         ("e5m2", "e5m2", False, "float_e5m2_t", "float_e5m2_t", "float"),
-         ("u8", "s8", False, "uint8_t", "int8_t", "int32_t"),
-         ("s8", "s8", True, "int8_t", "int8_t", "int32_t")]
+_E2M3 = "cutlass::detail::float_e2m3_unpacksmem_t"
+_E3M2 = "cutlass::detail::float_e3m2_unpacksmem_t"
+_E2M1 = "cutlass::detail::float_e2m1_unpacksmem_t"
+
+# (A, B, saturate, accumulator, CUTLASS A type, B type, C type)
+CASES = [("tf32", "tf32", False, "f32", "tfloat32_t", "tfloat32_t", "float"),
+         ("bf16", "bf16", False, "f32", "bfloat16_t", "bfloat16_t", "float"),
+         ("f16", "f16", False, "f32", "half_t", "half_t", "float"),
+         ("f16", "f16", False, "f16", "half_t", "half_t", "half_t"),
+         ("e4m3", "e5m2", False, "f32", "float_e4m3_t", "float_e5m2_t", "float"),
+         ("e5m2", "e5m2", False, "f16", "float_e5m2_t", "float_e5m2_t", "half_t"),
+         ("e2m3", "e2m1", False, "f32", _E2M3, _E2M1, "float"),
+         ("e3m2", "e4m3", False, "f16", _E3M2, "float_e4m3_t", "half_t"),
+         ("e2m1", "e3m2", False, "f32", _E2M1, _E3M2, "float"),
+         ("u8", "s8", False, "s32", "uint8_t", "int8_t", "int32_t"),
+         ("s8", "s8", True, "s32", "int8_t", "int8_t", "int32_t")]
 
 
 def test_instruction_descriptors_match_cutlass(tmp_path):
@@ -42,7 +55,7 @@ def test_instruction_descriptors_match_cutlass(tmp_path):
         pytest.skip("CUTLASS headers or nvcc not available")
     lines = ["#include <cstdio>", "#include <cute/arch/mma_sm100_desc.hpp>",
              "#include <cute/numeric/numeric_types.hpp>", "using namespace cute;", "int main() {"]
-    for _, _, sat, ta, tb, tc in CASES:
+    for _, _, sat, _, ta, tb, tc in CASES:
         s = "UMMA::ScaleIn::One, UMMA::ScaleIn::One, UMMA::Saturate::True" if sat else ""
         extra = (", " + s) if s else ""
         lines.append(f'  printf("%u\\n", uint32_t(UMMA::make_instr_desc<{ta}, {tb}, {tc}, 128, 16, '
@@ -54,28 +67,102 @@ def test_instruction_descriptors_match_cutlass(tmp_path):
     subprocess.run([nvcc, "-std=c++17", "-I", str(inc), "-o", str(exe), str(src)], check=True,
                    capture_output=True, timeout=600)
     want = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
-    got = [hwcheck.instr_desc(fa, fb, saturate=sat)[1] for fa, fb, sat, *_ in CASES]
+    got = [hwcheck.instr_desc(fa, fb, saturate=sat, d_type=d)[1] for fa, fb, sat, d, *_ in CASES]
     assert got == want
 
 
 def test_descriptor_and_shape_validation():
     assert hwcheck.instr_desc("tf32") == (0, 0x08040910)
     with pytest.raises(ValueError):
-        hwcheck.instr_desc("e2m1")
+        hwcheck.instr_desc("e8m0")
     with pytest.raises(ValueError):
         hwcheck.instr_desc("tf32", "bf16")
     with pytest.raises(ValueError):
+        hwcheck.instr_desc("f16", "bf16")
+    with pytest.raises(ValueError):
         hwcheck.instr_desc("bf16", saturate=True)
+    with pytest.raises(ValueError):
+        hwcheck.instr_desc("bf16", d_type="f16")
+    with pytest.raises(ValueError):
+        hwcheck.instr_desc("tf32", d_type="f16")
+    with pytest.raises(ValueError):
+        hwcheck.instr_desc("u8", d_type="f32")
     a, b, c = hwcheck.random_tiles("bf16", None, 2, 0)
     assert a.shape == (2, 128, 16) and b.shape == (2, 16, 16) and c.shape == (2, 128, 16)
+    a, b, c = hwcheck.random_tiles("e2m1", "e3m2", 2, 0, "f16")
+    assert a.shape == (2, 128, 32) and b.shape == (2, 32, 16) and int(c.max()) <= 0xFFFF
+
+
+def test_sub_byte_rows_have_the_f8f6f4_shared_memory_form():
+    rng = np.random.default_rng(3)
+    for fmt, bits in (("e2m1", 4), ("e2m3", 6), ("e3m2", 6)):
+        words = rng.integers(0, 1 << bits, size=(5, 32), dtype=np.uint32)
+        rows = hwcheck.smem_rows(words, fmt)
+        assert rows.shape == (5, 32)
+        used = 16 * bits // 8
+        for r in range(5):
+            for chunk in range(2):
+                body = rows[r, 16 * chunk:16 * chunk + used]
+                assert not rows[r, 16 * chunk + used:16 * (chunk + 1)].any()
+                bitstream = int.from_bytes(body.tobytes(), "little")
+                got = [(bitstream >> (bits * e)) & ((1 << bits) - 1) for e in range(16)]
+                assert got == list(words[r, 16 * chunk:16 * chunk + 16])
+    words = rng.integers(0, 256, size=(3, 32), dtype=np.uint32)
+    assert np.array_equal(hwcheck.smem_rows(words, "e4m3"), words.astype(np.uint8))
+
+
+def test_abi_rejects_descriptors_outside_the_documented_encodings():
+    """Every descriptor here is refused with T5E_ERR_INVALID by the host-side
+    check, before any CUDA call, so the test needs no GPU (the pointers are
+    aligned placeholders that are never dereferenced)."""
+    lib = nat.load()
+    fake = ctypes.c_void_p(1 << 20)
+    k_f16, d_f32 = hwcheck.instr_desc("f16")
+    k_f8, d_f8 = hwcheck.instr_desc("e4m3", "e2m1")
+    k_i8, d_i8 = hwcheck.instr_desc("s8", "u8")
+    k_tf, d_tf = hwcheck.instr_desc("tf32")
+    bad = [
+        (k_f16, d_f32 | (1 << 2)),                        # sparse
+        (k_f16, d_f32 | (1 << 15)),                       # A MN-major
+        (k_f16, d_f32 | (1 << 16)),                       # B MN-major
+        (k_f16, d_f32 | (1 << 13)),                       # negate A
+        (k_f16, d_f32 | (1 << 6)),                        # reserved bit
+        (k_f16, d_f32 | (1 << 30)),                       # max shift
+        (k_f16, (d_f32 & ~(0x3F << 17)) | (1 << 17)),     # N = 8
+        (k_f16, (d_f32 & ~(0x1F << 24)) | (4 << 24)),     # M = 64
+        (k_f16, d_f32 | (1 << 10)),                       # F16 A with BF16 B
+        (k_f16, d_f32 | (1 << 3)),                        # saturation on kind::f16
+        (k_f16, (d_f32 & ~(3 << 4)) | (2 << 4)),          # S32 accumulator on kind::f16
+        (k_f16, (d_f32 & ~(3 << 4)) | (1 << 7) | (1 << 10)),  # BF16 into an F16 accumulator
+        (k_f8, (d_f8 & ~(7 << 7)) | (2 << 7)),            # format code 2 on kind::f8f6f4
+        (k_f8, (d_f8 & ~(7 << 10)) | (6 << 10)),          # format code 6 on kind::f8f6f4
+        (k_tf, d_tf & ~(3 << 4)),                         # F16 accumulator on kind::tf32
+        (k_i8, (d_i8 & ~(3 << 4)) | (1 << 4)),            # F32 accumulator on kind::i8
+        (k_i8, d_i8 | (2 << 7)),                          # format code 3 on kind::i8
+        (7, d_f32),                                       # unknown kind
+        (k_f8, d_i8),                                     # i8 descriptor under kind::f8f6f4
+    ]
+    for kind, desc in bad:
+        rc = lib.t5e_tcgen05_tiles(kind, desc, fake, fake, fake, fake, 1, fake, None)
+        assert rc == nat.ERR_INVALID, (kind, hex(desc), rc)
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("fa,fb,sat", [(p[0], p[1], p[2]) for p in hwcheck.PAIRS],
-                         ids=[f"{p[0]}x{p[1]}{'-sat' if p[2] else ''}" for p in hwcheck.PAIRS])
-def test_tcgen05_hardware_equals_emulator(fa, fb, sat):
-    a, b, c = hwcheck.random_tiles(fa, fb, 48, 17)
-    r = hwcheck.cross_check(a, b, c, fa, fb, saturate=sat)
+@pytest.mark.parametrize("fa,fb,sat,d", hwcheck.PAIRS,
+                         ids=[f"{p[0]}x{p[1]}-{p[3]}{'-sat' if p[2] else ''}" for p in hwcheck.PAIRS])
+def test_tcgen05_hardware_equals_emulator(fa, fb, sat, d):
+    a, b, c = hwcheck.random_tiles(fa, fb, 48, 17, d)
+    r = hwcheck.cross_check(a, b, c, fa, fb, saturate=sat, d_type=d)
+    if fa == fb == d == "f16":
+        # the raw half has NaN and infinite results: the hardware writes F16
+        # special words there, the reference its F32 ones; nothing else differs
+        assert r["reference_f32_special_words"] > 0
+        hw = r["hardware"].reshape(-1)
+        emu = r["emulator"].reshape(-1)
+        special = np.isin(emu, list(hwcheck.REFERENCE_F32_SPECIAL_FOR_F16.values()))
+        assert np.isin(hw[special], list(hwcheck.REFERENCE_F32_SPECIAL_FOR_F16)).all()
+    else:
+        assert r["reference_f32_special_words"] == 0
     assert r["mismatches"] == 0, (f"{r['mismatches']} of {r['cases']} words differ; first cases {r['first']}: "
                                   f"hardware {[hex(int(x)) for x in r['hardware'].reshape(-1)[r['first']]]} "
                                   f"emulator {[hex(int(x)) for x in r['emulator'].reshape(-1)[r['first']]]}")
