@@ -433,8 +433,23 @@ def _pinned(x) -> bool:
 
 # Batches at least this large, with every per-case array in pinned host
 # memory, are streamed through the GPU in chunks (see _pipelined_batch).
+# Each chunk costs tens of microseconds of host-side issue, so a few large
+# chunks keep the host-to-device copies back to back.
 PIPELINE_MIN_CASES = 1 << 16
-PIPELINE_CHUNKS = 8
+PIPELINE_CHUNKS = 4
+
+_COPY_STREAMS: dict = {}
+
+
+def _copy_streams(dev):
+    """The (upload, download) streams of a device, created once."""
+    import torch
+
+    key = dev.index if dev.index is not None else torch.cuda.current_device()
+    pair = _COPY_STREAMS.get(key)
+    if pair is None:
+        pair = _COPY_STREAMS[key] = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+    return pair
 
 
 def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n, dev, out, check, meta_error,
@@ -447,8 +462,14 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
     import torch
 
     comp = torch.cuda.current_stream(dev)
-    up = torch.cuda.Stream(dev)
-    down = torch.cuda.Stream(dev)
+    up, down = _copy_streams(dev)
+    # the device buffers below come from the allocator on the current stream:
+    # the uploads wait for whatever that stream still has queued
+    up.wait_stream(comp)
+    # per-case status bytes only exist for sparse selections: every other
+    # per-case error (scale cover, K range) is decided for the whole batch on
+    # the host before the launch
+    check = check and sparse != 0
     a_dev = torch.empty(a.data.shape, dtype=torch.uint8, device=dev)
     b_dev = torch.empty(b.data.shape, dtype=torch.uint8, device=dev)
     c_dev = torch.empty(c.shape, dtype=c.dtype, device=dev)
