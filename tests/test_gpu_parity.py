@@ -114,6 +114,33 @@ def test_configurations_match_reference_and_oracle(name, golden_paths):
     assert_words_equal(gpu_cases(big), oracle.eval_cases(big), name + " 2^17 vs oracle")
 
 
+MX_SUB_BYTE = ("e2m3", "e3m2", "e2m1")
+
+
+@pytest.mark.parametrize("fa,fb", [(fa, fb) for fa in MX_SUB_BYTE for fb in MX_SUB_BYTE])
+def test_mxf8f6f4_sub_byte_kernel_matches_oracle(fa, fb):
+    """The dedicated MXF8F6F4 kernel for every E2M3/E3M2/E2M1 pair (K=32, one
+    UE8M0 scale per operand): uniform codes, scales over the whole UE8M0 range
+    (0xFF, NaN, included), C half raw words and half finite words.  C then
+    often sets a window far above the products, so that every product is
+    truncated on its own (the kernel's queued pass) as well as summed exactly."""
+    rng = np.random.default_rng(2024 + 7 * len(fa) + len(fb))
+    n = 1 << 14
+    bits = {"e2m3": 6, "e3m2": 6, "e2m1": 4}
+    a = rng.integers(0, 1 << bits[fa], (n, 32), dtype=np.uint64).astype(np.uint32)
+    b = rng.integers(0, 1 << bits[fb], (n, 32), dtype=np.uint64).astype(np.uint32)
+    sa = rng.integers(0, 256, (n, 1), dtype=np.uint64).astype(np.uint32)
+    sb = rng.integers(0, 256, (n, 1), dtype=np.uint64).astype(np.uint32)
+    c = np.concatenate([workloads.f32_words(rng, n // 2), workloads.f32_words(rng, n - n // 2, True)])
+    desc = dict(a_format=fa, b_format=fb, scaling="ue8m0", kind="mxf8f6f4")
+    got = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, **desc)
+    want, st = oracle.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, **desc)
+    assert not st.any()
+    assert_words_equal(got, want, f"{fa}x{fb}")
+    generic = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, generic=True, **desc)
+    assert_words_equal(generic, want, f"{fa}x{fb} generic")
+
+
 # ------------------------------------------------------------ edge cases
 
 EDGE_DESCS = [
