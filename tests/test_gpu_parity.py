@@ -339,6 +339,24 @@ def test_matrix_configuration_tiles_fast_equals_generic(desc, k):
     assert_words_equal(fast.reshape(-1)[idx], want, f"{desc} tiles sample vs oracle")
 
 
+@pytest.mark.parametrize("desc,k", [(dict(a_format="bf16"), 16), (dict(a_format="f16", d_type="f16"), 16)])
+def test_largest_staged_tiles_fast_equals_generic(desc, k):
+    """The largest tile the specialised kernel stages (M=256 rows of A,
+    N=4096 columns: 50 KB of shared memory, above the default 48 KB limit)
+    equals the generic kernel."""
+    d = full_desc(desc)
+    rng = np.random.Generator(np.random.PCG64(909))
+    t, m, n = 1, 256, 4096
+    fmt = t5.normalize_format(d["a_format"])
+    a = _edge_words(fmt, rng, t * m, k).reshape(t, m, k)
+    b = _edge_words(fmt, rng, t * n, k).reshape(t, n, k).transpose(0, 2, 1).copy()
+    c = (workloads.f16_words(rng, t * m * n) if d["d_type"] == "f16" else workloads.f32_words(rng, t * m * n))
+    kw = {kk: d[kk] for kk in KEYS}
+    fast = t5.mma_batch(a, b, c.reshape(t, m, n), **kw)
+    generic = t5.mma_batch(a, b, c.reshape(t, m, n), generic=True, **kw)
+    assert_words_equal(fast.reshape(-1), generic.reshape(-1), f"{desc} 256x4096 tile fast vs generic")
+
+
 def test_matrix_sparse_shares_metadata():
     rng = np.random.Generator(np.random.PCG64(5))
     a = rng.integers(0, 256, size=(8, 64), dtype=np.uint32)
