@@ -4,6 +4,8 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "t5e.h"
 
 namespace t5e {
@@ -29,5 +31,25 @@ void set_cuda_error(const char* what, cudaError_t err);
 
 // Grid size for a grid-stride loop over n items.
 int grid_for(uint64_t n, int block);
+
+// Raises Kernel's dynamic shared-memory limit to `bytes` on the current
+// device, once per device and kernel (one flag array per kernel; host
+// threads may race to set it, which is harmless: the attribute value is the
+// same).  Returns T5E_OK or T5E_ERR_CUDA.
+template <auto Kernel>
+int raise_smem_limit(int bytes, const char* what) {
+  static std::atomic<bool> done[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) dev = -1;
+  const bool cached = dev >= 0 && dev < 64;
+  if (cached && done[dev].load(std::memory_order_acquire)) return T5E_OK;
+  const cudaError_t err = cudaFuncSetAttribute(Kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (err != cudaSuccess) {
+    set_cuda_error(what, err);
+    return T5E_ERR_CUDA;
+  }
+  if (cached) done[dev].store(true, std::memory_order_release);
+  return T5E_OK;
+}
 
 }  // namespace t5e

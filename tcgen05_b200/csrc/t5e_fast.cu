@@ -395,17 +395,10 @@ template <int AF, int BF, bool F16D, bool SCALED>
 int launch_raw(const t5e_batch& B, cudaStream_t stream) {
   auto kern = raw_window_kernel<AF, BF, F16D, SCALED>;
   const int smem = kLutBytes + kWarps * kQueue * 4;
+  const int rc = raise_smem_limit<raw_window_kernel<AF, BF, F16D, SCALED>>(smem, "raw_window_kernel attribute");
+  if (rc != T5E_OK) return rc;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
-  static bool configured[64] = {};  // the attribute is set once per device and kernel
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    const cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (err != cudaSuccess) {
-      set_cuda_error("raw_window_kernel attribute", err);
-      return T5E_ERR_CUDA;
-    }
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const uint64_t tiles = (B.n + 31) / 32;
   const uint64_t want = (tiles + kWarps - 1) / kWarps;

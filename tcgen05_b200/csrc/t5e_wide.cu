@@ -333,17 +333,10 @@ int launch_tiles(const t5e_batch& B, int floor_raw, cudaStream_t stream) {
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  static bool configured[64] = {};  // above 48 KB of dynamic shared memory, once per device
-  if (dev < 0 || dev >= 64 || !configured[dev]) {
-    const cudaError_t err = cudaFuncSetAttribute(wide_tile_kernel<F, F16D>,
-                                                 cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 (2 * kTileRowsMax * K + kTileRowsMax + kTileColsMax) * 4);
-    if (err != cudaSuccess) {
-      set_cuda_error("wide_tile_kernel attribute", err);
-      return T5E_ERR_CUDA;
-    }
-    if (dev >= 0 && dev < 64) configured[dev] = true;
-  }
+  // above the default 48 KB for the largest staged tiles
+  const int rc = raise_smem_limit<wide_tile_kernel<F, F16D>>((2 * kTileRowsMax * K + kTileRowsMax + kTileColsMax) * 4,
+                                                             "wide_tile_kernel attribute");
+  if (rc != T5E_OK) return rc;
   const int threads = B.tile_n >= kThreads ? kThreads : ((B.tile_n + 31) / 32) * 32;
   if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, wide_tile_kernel<F, F16D>, threads, smem) !=
           cudaSuccess ||
