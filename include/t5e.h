@@ -203,6 +203,21 @@ enum { T5E_HW_TF32 = 0, T5E_HW_F16 = 1, T5E_HW_F8F6F4 = 2, T5E_HW_I8 = 3 };
 int t5e_tcgen05_tiles(int32_t kind, uint32_t idesc, const void* a, const void* b, const uint32_t* c, uint32_t* d,
                       uint64_t tiles, int32_t* error, void* stream);
 
+/* The same for the block-scaled kinds (no counterpart in the reference's
+ * model package either): tiles of M = 128, N = 128 and one instruction's K
+ * (32 f8f6f4 elements, or 64 packed E2M1), 32-byte K-major rows:
+ *   a: tiles*128 rows, b: tiles*128 rows (the columns of B), c, d:
+ *   tiles*128*128 F32 words (row-major), 16-byte aligned;
+ *   scale_a, scale_b: tiles*128 words, one per row of A / column of B, whose
+ *   byte j is the scale of K block j (one block for kind::mxf8f6f4, two for
+ *   T5E_HW_MXF4 and T5E_HW_MXF4NVF4_2X, four for T5E_HW_MXF4NVF4_4X).
+ * `idesc` is the block-scaled instruction descriptor (formats, N, M, scale
+ * format; scale factor ids 0); others are rejected before any launch. */
+enum { T5E_HW_MXF8F6F4 = 4, T5E_HW_MXF4 = 5, T5E_HW_MXF4NVF4_2X = 6, T5E_HW_MXF4NVF4_4X = 7 };
+int t5e_tcgen05_block_scaled_tiles(int32_t kind, uint32_t idesc, const void* a, const void* b, const uint32_t* c,
+                                   uint32_t* d, const uint32_t* scale_a, const uint32_t* scale_b, uint64_t tiles,
+                                   int32_t* error, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -113,6 +113,7 @@ EXPORTED = (
     "t5e_pack_rows",
     "t5e_sparse_active",
     "t5e_tcgen05_tiles",
+    "t5e_tcgen05_block_scaled_tiles",
 )
 
 _lib = None
@@ -151,6 +152,11 @@ def load() -> ctypes.CDLL:
     lib.t5e_tcgen05_tiles.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,
                                       ctypes.c_void_p]
+    lib.t5e_tcgen05_block_scaled_tiles.restype = ctypes.c_int
+    lib.t5e_tcgen05_block_scaled_tiles.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
+                                                   ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                   ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,
+                                                   ctypes.c_void_p]
     version = lib.t5e_abi_version()
     if version != ABI_VERSION:
         raise NativeLibraryError(f"{LIB_PATH} has ABI version {version}, expected {ABI_VERSION}; rebuild it")

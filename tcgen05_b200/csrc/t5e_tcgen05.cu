@@ -197,6 +197,188 @@ int launch(const void* a, const void* b, const uint32_t* c, uint32_t* d, uint64_
   return kernel_status("tcgen05_tile_kernel launch");
 }
 
+
+// ---- block-scaled kinds ---------------------------------------------------
+//
+// kind::mxf8f6f4 (UE8M0, one scale per 32 K), kind::mxf4 (E2M1, UE8M0, two
+// scales per 64 K) and kind::mxf4nvf4 (E2M1, two UE8M0 or four UE4M3/UE8M0
+// scales per 64 K) on tiles of M = 128, N = 128 and one instruction's K (32
+// elements of f8f6f4, 64 packed E2M1), 32-byte K-major operand rows in the same
+// shared-memory layout as above.  The scale factors live in tensor memory in
+// the layout the instruction reads for cta_group::1: the factor of row (or
+// column) r sits in lane r % 32 of every 32-lane subpartition, column r / 32
+// of the scale-factor area, byte = the scale block along K (scale factor
+// id 0).  One CTA of 128 threads per tile allocates 256 TMEM columns (D in
+// 0-127, A scale factors at 192, B scale factors at 224); its dynamic shared
+// memory request keeps at most two CTAs on an SM, so an allocation never
+// waits.
+constexpr int kBsRows = 128, kBsCols = 128, kBsTmemCols = 256, kBsSfaCol = 192, kBsSfbCol = 224;
+constexpr int kBsSmemBytes = 96 * 1024;
+
+__device__ __forceinline__ void tmem_st32(uint32_t addr, const uint32_t (&v)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+               :: "r"(addr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t addr, uint32_t (&v)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31]) : "r"(addr) : "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ void mma_block_scaled(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc,
+                                                 uint32_t tsfa, uint32_t tsfb) {
+  const uint32_t accumulate = 1;
+  if constexpr (KIND == T5E_HW_MXF8F6F4) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+  } else if constexpr (KIND == T5E_HW_MXF4) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+  } else if constexpr (KIND == T5E_HW_MXF4NVF4_2X) {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+  } else {
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}\n"
+                 :: "r"(tmem_d), "l"(da), "l"(db), "r"(idesc), "r"(accumulate), "r"(tsfa), "r"(tsfb));
+  }
+}
+
+template <int KIND>
+__global__ void __launch_bounds__(kBsRows) tcgen05_block_scaled_kernel(
+    const uint8_t* __restrict__ A, const uint8_t* __restrict__ B, const uint32_t* __restrict__ C,
+    uint32_t* __restrict__ D, const uint32_t* __restrict__ SFA, const uint32_t* __restrict__ SFB, uint32_t idesc,
+    uint32_t tiles, int* error) {
+  extern __shared__ __align__(128) uint8_t smem_bs[];
+  uint8_t* sA = smem_bs;                     // 128 rows of 32 bytes, core-matrix layout
+  uint8_t* sB = smem_bs + kBsRows * kRowBytes;
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(smem_bs + 2 * kBsRows * kRowBytes);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mbar + 1);
+  const int t = threadIdx.x, warp = t >> 5, l = t & 31;
+  const uint32_t bar = smem_u32(mbar);
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 :: "r"(smem_u32(tmem_slot)), "r"(kBsTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  if (t == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(1));
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  uint32_t phase = 0;
+  for (uint32_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    // row t of A and of B into the core-matrix layout
+    const uint4* ga = reinterpret_cast<const uint4*>(A + ((size_t)tile * kBsRows + t) * kRowBytes);
+    const uint4* gb = reinterpret_cast<const uint4*>(B + ((size_t)tile * kBsCols + t) * kRowBytes);
+    const uint4 a0 = __ldg(ga), a1 = __ldg(ga + 1), b0 = __ldg(gb), b1 = __ldg(gb + 1);
+    *reinterpret_cast<uint4*>(sA + (t >> 3) * 256 + (t & 7) * 16) = a0;
+    *reinterpret_cast<uint4*>(sA + (t >> 3) * 256 + 128 + (t & 7) * 16) = a1;
+    *reinterpret_cast<uint4*>(sB + (t >> 3) * 256 + (t & 7) * 16) = b0;
+    *reinterpret_cast<uint4*>(sB + (t >> 3) * 256 + 128 + (t & 7) * 16) = b1;
+    // C row t into lane t, columns 0-127
+    const uint4* crow = reinterpret_cast<const uint4*>(C + ((size_t)tile * kBsRows + t) * kBsCols);
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t v[32];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const uint4 x = __ldg(crow + ch * 8 + q);
+        v[4 * q] = x.x; v[4 * q + 1] = x.y; v[4 * q + 2] = x.z; v[4 * q + 3] = x.w;
+      }
+      tmem_st32(lane_base + (uint32_t)(ch * 32), v);
+    }
+    // scale factors: column c holds the factors of rows 32 c + (lane % 32),
+    // the same in every subpartition
+    uint32_t fa[4], fb[4];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      fa[c] = __ldg(SFA + (size_t)tile * kBsRows + 32 * c + l);
+      fb[c] = __ldg(SFB + (size_t)tile * kBsCols + 32 * c + l);
+    }
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};"
+                 :: "r"(lane_base + (uint32_t)kBsSfaCol), "r"(fa[0]), "r"(fa[1]), "r"(fa[2]), "r"(fa[3]) : "memory");
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};"
+                 :: "r"(lane_base + (uint32_t)kBsSfbCol), "r"(fb[0]), "r"(fb[1]), "r"(fb[2]), "r"(fb[3]) : "memory");
+    asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    if (t == 0) {
+      mma_block_scaled<KIND>(tmem, smem_desc(smem_u32(sA)), smem_desc(smem_u32(sB)), idesc,
+                             tmem + (uint32_t)kBsSfaCol, tmem + (uint32_t)kBsSfbCol);
+      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+                   :: "r"(bar) : "memory");
+    }
+    const bool ok = wait_phase(bar, phase);
+    phase ^= 1u;
+    if (__syncthreads_or(!ok)) {  // the product never arrived: record it and stop
+      if (t == 0) atomicExch(error, 1);
+      break;
+    }
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+    uint4* drow = reinterpret_cast<uint4*>(D + ((size_t)tile * kBsRows + t) * kBsCols);
+#pragma unroll
+    for (int ch = 0; ch < 4; ++ch) {
+      uint32_t v[32];
+      tmem_ld32(lane_base + (uint32_t)(ch * 32), v);
+      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+      for (int q = 0; q < 8; ++q) drow[ch * 8 + q] = make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+    __syncthreads();  // shared memory and TMEM are reused by the next tile
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp == 0) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" :: "r"(tmem), "r"(kBsTmemCols));
+  }
+}
+
+// Documented block-scaled encodings for M = 128, N = 128, dense K-major
+// operands, scale factor ids 0 and the default K: E2M1 (code 1) for the mxf4
+// kinds, the f8f6f4 codes for mxf8f6f4, UE8M0 scales (bit 23 set) except for
+// the four-scale mxf4nvf4 form, which also takes UE4M3.
+bool block_scaled_descriptor_ok(int32_t kind, uint32_t idesc) {
+  const uint32_t fields = (7u << 7) | (7u << 10) | (0x3Fu << 17) | (1u << 23) | (0x1Fu << 24);
+  if ((idesc & ~fields) != 0u) return false;
+  if (((idesc >> 24) & 0x1Fu) != 8u || ((idesc >> 17) & 0x3Fu) != 16u) return false;
+  const uint32_t af = (idesc >> 7) & 7u, bf = (idesc >> 10) & 7u, ue8m0 = (idesc >> 23) & 1u;
+  auto f8f6f4 = [](uint32_t f) { return f == 0u || f == 1u || f == 3u || f == 4u || f == 5u; };
+  switch (kind) {
+    case T5E_HW_MXF8F6F4: return f8f6f4(af) && f8f6f4(bf) && ue8m0;
+    case T5E_HW_MXF4: return af == 1u && bf == 1u && ue8m0;
+    case T5E_HW_MXF4NVF4_2X: return af == 1u && bf == 1u && ue8m0;
+    case T5E_HW_MXF4NVF4_4X: return af == 1u && bf == 1u;
+    default: return false;
+  }
+}
+
+template <int KIND>
+int launch_block_scaled(const void* a, const void* b, const uint32_t* c, uint32_t* d, const uint32_t* sfa,
+                        const uint32_t* sfb, uint64_t tiles, uint32_t idesc, int* error, cudaStream_t stream) {
+  const int rc = raise_smem_limit<tcgen05_block_scaled_kernel<KIND>>(kBsSmemBytes, "tcgen05 block-scaled attribute");
+  if (rc != T5E_OK) return rc;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const uint64_t cap = (uint64_t)sms * 2u;
+  const int grid = (int)(tiles < cap ? tiles : cap);
+  tcgen05_block_scaled_kernel<KIND><<<grid, kBsRows, kBsSmemBytes, stream>>>(
+      static_cast<const uint8_t*>(a), static_cast<const uint8_t*>(b), c, d, sfa, sfb, idesc, (uint32_t)tiles, error);
+  return kernel_status("tcgen05_block_scaled_kernel launch");
+}
+
 }  // namespace hw
 }  // namespace t5e
 
@@ -215,6 +397,31 @@ extern "C" int t5e_tcgen05_tiles(int32_t kind, uint32_t idesc, const void* a, co
     case T5E_HW_F16: return launch<T5E_HW_F16>(a, b, c, d, tiles, idesc, err, s);
     case T5E_HW_F8F6F4: return launch<T5E_HW_F8F6F4>(a, b, c, d, tiles, idesc, err, s);
     case T5E_HW_I8: return launch<T5E_HW_I8>(a, b, c, d, tiles, idesc, err, s);
+    default: return T5E_ERR_INVALID;
+  }
+}
+
+extern "C" int t5e_tcgen05_block_scaled_tiles(int32_t kind, uint32_t idesc, const void* a, const void* b,
+                                              const uint32_t* c, uint32_t* d, const uint32_t* scale_a,
+                                              const uint32_t* scale_b, uint64_t tiles, int32_t* error,
+                                              void* stream) {
+  using namespace t5e::hw;
+  if (tiles == 0) return T5E_OK;
+  if (!a || !b || !c || !d || !scale_a || !scale_b || !error || tiles >= (1ull << 31)) return T5E_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) | reinterpret_cast<uintptr_t>(c) |
+       reinterpret_cast<uintptr_t>(d)) % 16 != 0)
+    return T5E_ERR_INVALID;
+  if ((reinterpret_cast<uintptr_t>(scale_a) | reinterpret_cast<uintptr_t>(scale_b)) % 4 != 0) return T5E_ERR_INVALID;
+  if (!block_scaled_descriptor_ok(kind, idesc)) return T5E_ERR_INVALID;
+  int* err = reinterpret_cast<int*>(error);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (kind) {
+    case T5E_HW_MXF8F6F4: return launch_block_scaled<T5E_HW_MXF8F6F4>(a, b, c, d, scale_a, scale_b, tiles, idesc, err, s);
+    case T5E_HW_MXF4: return launch_block_scaled<T5E_HW_MXF4>(a, b, c, d, scale_a, scale_b, tiles, idesc, err, s);
+    case T5E_HW_MXF4NVF4_2X:
+      return launch_block_scaled<T5E_HW_MXF4NVF4_2X>(a, b, c, d, scale_a, scale_b, tiles, idesc, err, s);
+    case T5E_HW_MXF4NVF4_4X:
+      return launch_block_scaled<T5E_HW_MXF4NVF4_4X>(a, b, c, d, scale_a, scale_b, tiles, idesc, err, s);
     default: return T5E_ERR_INVALID;
   }
 }

@@ -202,6 +202,160 @@ PAIRS = (("tf32", "tf32", False, "f32"), ("bf16", "bf16", False, "f32"), ("f16",
     + (("u8", "s8", False, "s32"), ("s8", "u8", False, "s32"), ("u8", "u8", False, "s32"), ("s8", "s8", True, "s32"))
 
 
+# ---- block-scaled kinds ------------------------------------------------
+#
+# Tiles of M = 128, N = 128 and one instruction's K: 32 f8f6f4 elements
+# (kind::mxf8f6f4, one UE8M0 scale per row and column), or 64 packed E2M1
+# (kind::mxf4: two UE8M0 scales; kind::mxf4nvf4: two UE8M0 or four UE4M3 /
+# UE8M0 scales).  The emulator side is the matching make_model descriptor:
+# scaling, kind and scale_vec as the reference names them.
+BS_N = 128
+BS_KINDS = {"mxf8f6f4": 4, "mxf4": 5, "mxf4nvf4-2x": 6, "mxf4nvf4-4x": 7}
+BS_K = {"mxf8f6f4": 32, "mxf4": 64, "mxf4nvf4-2x": 64, "mxf4nvf4-4x": 64}
+BS_BLOCKS = {"mxf8f6f4": 1, "mxf4": 2, "mxf4nvf4-2x": 2, "mxf4nvf4-4x": 4}
+MXF4_E2M1 = 1  # the E2M1 code of the mxf4 kinds (packed operands)
+
+
+def block_scaled_desc(kind: str, a_format: str, b_format: str | None = None, scale: str = "ue8m0") -> tuple[int, int]:
+    """(kind id, block-scaled instruction descriptor): formats at bits 7-9 and
+    10-12, N/8 at 17-22, the scale format at bit 23 (1 = UE8M0, 0 = UE4M3),
+    M/16 at 24-28, scale factor ids 0."""
+    b_format = b_format or a_format
+    if kind not in BS_KINDS:
+        raise ValueError(f"unknown block-scaled kind {kind}")
+    if kind == "mxf8f6f4":
+        if a_format not in FORMAT_CODES or KINDS.get(a_format) != 2 or KINDS.get(b_format) != 2:
+            raise ValueError("kind::mxf8f6f4 takes f8f6f4 operands")
+        fa, fb = FORMAT_CODES[a_format], FORMAT_CODES[b_format]
+    else:
+        if a_format != "e2m1" or b_format != "e2m1":
+            raise ValueError(f"kind::{kind} takes E2M1 operands")
+        fa = fb = MXF4_E2M1
+    if scale not in ("ue8m0", "ue4m3") or (scale == "ue4m3" and kind != "mxf4nvf4-4x"):
+        raise ValueError(f"{kind} does not take {scale} scales")
+    desc = (fa << 7) | (fb << 10) | ((BS_N >> 3) << 17) | ((1 if scale == "ue8m0" else 0) << 23) | ((M >> 4) << 24)
+    return BS_KINDS[kind], desc
+
+
+def block_scaled_model_args(kind: str, scale: str) -> dict:
+    """make_model keywords of the emulator path a block-scaled kind runs."""
+    if kind == "mxf8f6f4":
+        return dict(scaling="ue8m0", kind="mxf8f6f4")
+    if kind == "mxf4":
+        return dict(scaling="ue8m0", kind="mxf4")
+    if kind == "mxf4nvf4-2x":
+        return dict(scaling="ue8m0", kind="mxf4nvf4", scale_vec=2)
+    return dict(scaling="ue4m3", scale_vec=4) if scale == "ue4m3" else dict(scaling="ue8m0", kind="mxf4nvf4",
+                                                                           scale_vec=4)
+
+
+def block_scaled_rows(words, fmt: str, kind: str) -> np.ndarray:
+    """[R, K] words -> [R, 32] operand bytes: the f8f6f4 form for
+    kind::mxf8f6f4, 64 packed E2M1 otherwise."""
+    if kind == "mxf8f6f4":
+        return smem_rows(words, fmt)
+    w = np.asarray(words, dtype=np.uint32)
+    out = packing.pack_rows(w, nat.FORMAT_IDS["e2m1"])
+    if out.shape[1] != 32:
+        raise ValueError("mxf4 rows hold 64 E2M1 elements")
+    return out
+
+
+def scale_words(scales) -> np.ndarray:
+    """[R, blocks] scale bytes -> R words, block j in byte j."""
+    s = np.asarray(scales, dtype=np.uint32)
+    w = np.zeros(s.shape[0], dtype=np.uint32)
+    for j in range(s.shape[1]):
+        w |= (s[:, j] & 0xFF) << (8 * j)
+    return w
+
+
+def hardware_block_scaled_tiles(a, b, c, scale_a, scale_b, kind: str, a_format: str, b_format: str | None = None,
+                                scale: str = "ue8m0", device=None):
+    """D words of T block-scaled tiles computed by tcgen05.mma: a [T, 128, K],
+    b [T, K, 128] (row-major B), c [T, 128, 128] F32 words, scale_a
+    [T, 128, blocks] (per A row), scale_b [T, 128, blocks] (per B column)."""
+    import torch
+
+    b_format = b_format or a_format
+    kid, desc = block_scaled_desc(kind, a_format, b_format, scale)
+    k, blocks = BS_K[kind], BS_BLOCKS[kind]
+    a = np.asarray(a, dtype=np.uint32)
+    b = np.asarray(b, dtype=np.uint32)
+    t = a.shape[0]
+    shapes = (a.shape, b.shape, np.asarray(c).shape, np.asarray(scale_a).shape, np.asarray(scale_b).shape)
+    if shapes != ((t, M, k), (t, k, BS_N), (t, M, BS_N), (t, M, blocks), (t, BS_N, blocks)):
+        raise ValueError(f"tiles must be A [T,{M},{k}], B [T,{k},{BS_N}], C [T,{M},{BS_N}], scales [T,128,{blocks}]")
+    dev = runtime.require_device(device)
+    a_dev = runtime.to_device(block_scaled_rows(a.reshape(t * M, k), a_format, kind), dev)
+    b_dev = runtime.to_device(block_scaled_rows(np.ascontiguousarray(b.transpose(0, 2, 1)).reshape(t * BS_N, k),
+                                                b_format, kind), dev)
+    c_dev = runtime.to_device(np.asarray(c, dtype=np.uint32).reshape(-1), dev)
+    sa_dev = runtime.to_device(scale_words(np.asarray(scale_a).reshape(t * M, blocks)), dev)
+    sb_dev = runtime.to_device(scale_words(np.asarray(scale_b).reshape(t * BS_N, blocks)), dev)
+    d_dev = torch.zeros(t * M * BS_N, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = nat.load()
+    stream = ctypes.c_void_p(runtime.current_stream_handle(dev))
+    rc = lib.t5e_tcgen05_block_scaled_tiles(kid, desc, a_dev.data_ptr(), b_dev.data_ptr(), c_dev.data_ptr(),
+                                            d_dev.data_ptr(), sa_dev.data_ptr(), sb_dev.data_ptr(), t,
+                                            err.data_ptr(), stream)
+    nat.check(rc, "t5e_tcgen05_block_scaled_tiles")
+    torch.cuda.synchronize(dev)
+    if int(err.item()):
+        raise RuntimeError("a tcgen05.mma product did not complete within the kernel's bounded wait")
+    return d_dev.cpu().numpy().view(np.uint32).reshape(t, M, BS_N)
+
+
+def cross_check_block_scaled(a, b, c, scale_a, scale_b, kind: str, a_format: str, b_format: str | None = None,
+                             scale: str = "ue8m0", device=None) -> dict:
+    """Hardware and emulator words of the same block-scaled tiles."""
+    from .simulator import mma_batch
+
+    b_format = b_format or a_format
+    hw = hardware_block_scaled_tiles(a, b, c, scale_a, scale_b, kind, a_format, b_format, scale, device=device)
+    emu = mma_batch(a, b, c, a_format=a_format, b_format=None if b_format == a_format else b_format,
+                    scale_a=scale_a, scale_b=scale_b, device=device, **block_scaled_model_args(kind, scale))
+    emu = np.asarray(emu, dtype=np.uint32)
+    diff = np.flatnonzero(hw.reshape(-1) != emu.reshape(-1))
+    return {"kind": kind, "a_format": a_format, "b_format": b_format, "scale": scale, "cases": int(hw.size),
+            "mismatches": int(diff.size), "first": [int(i) for i in diff[:8]], "hardware": hw, "emulator": emu}
+
+
+def random_block_scaled_tiles(kind: str, a_format: str, b_format: str | None, tiles: int, seed: int,
+                              scale: str = "ue8m0"):
+    """Tiles as random_tiles draws them, plus scales over the reference
+    generators' ranges: UE8M0 over all 256 bytes (0xFF is NaN), UE4M3 over
+    0x00-0x7F (0x7F is NaN)."""
+    from . import workloads
+
+    b_format = b_format or a_format
+    k, blocks = BS_K[kind], BS_BLOCKS[kind]
+    rng = np.random.Generator(np.random.PCG64(seed))
+    half = tiles // 2
+
+    def words(fmt, n):
+        raw = workloads.format_words(fmt, rng, half * n)
+        fin = workloads.format_words(fmt, rng, (tiles - half) * n, True)
+        return np.concatenate([raw, fin]).astype(np.uint32)
+
+    a = words(a_format, M * k).reshape(tiles, M, k)
+    b = words(b_format, k * BS_N).reshape(tiles, k, BS_N)
+    c = np.concatenate([workloads.f32_words(rng, half * M * BS_N),
+                        workloads.f32_words(rng, (tiles - half) * M * BS_N, True)]).astype(np.uint32)
+    top = 256 if scale == "ue8m0" else 128
+    sa = rng.integers(0, top, size=(tiles, M, blocks), dtype=np.uint64).astype(np.uint32)
+    sb = rng.integers(0, top, size=(tiles, BS_N, blocks), dtype=np.uint64).astype(np.uint32)
+    return a, b, c.reshape(tiles, M, BS_N), sa, sb
+
+
+# (kind, A format, B format, scale format): every mxf8f6f4 operand pair and
+# every mxf4 / mxf4nvf4 form
+BS_PAIRS = tuple(("mxf8f6f4", fa, fb, "ue8m0") for fa, fb in itertools.product(F8F6F4, F8F6F4)) + (
+    ("mxf4", "e2m1", "e2m1", "ue8m0"), ("mxf4nvf4-2x", "e2m1", "e2m1", "ue8m0"),
+    ("mxf4nvf4-4x", "e2m1", "e2m1", "ue8m0"), ("mxf4nvf4-4x", "e2m1", "e2m1", "ue4m3"))
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--tiles", type=int, default=64)
@@ -213,8 +367,16 @@ def main(argv=None) -> int:
         r = cross_check(a, b, c, fa, fb, saturate=sat, d_type=d)
         failed += r["mismatches"] != 0
         print(json.dumps({k: v for k, v in r.items() if k not in ("hardware", "emulator")}), flush=True)
-    print(json.dumps({"pairs": len(PAIRS), "pairs_with_mismatches": failed}), flush=True)
-    return 1 if failed else 0
+    bs_failed = 0
+    for i, (kind, fa, fb, scale) in enumerate(BS_PAIRS):
+        a, b, c, sa, sb = random_block_scaled_tiles(kind, fa, fb, max(2, args.tiles // 8), args.seed + 1000 + i,
+                                                    scale)
+        r = cross_check_block_scaled(a, b, c, sa, sb, kind, fa, fb, scale)
+        bs_failed += r["mismatches"] != 0
+        print(json.dumps({k: v for k, v in r.items() if k not in ("hardware", "emulator")}), flush=True)
+    print(json.dumps({"pairs": len(PAIRS), "pairs_with_mismatches": failed, "block_scaled_pairs": len(BS_PAIRS),
+                      "block_scaled_pairs_with_mismatches": bs_failed}), flush=True)
+    return 1 if failed or bs_failed else 0
 
 
 if __name__ == "__main__":

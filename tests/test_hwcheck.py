@@ -166,3 +166,86 @@ def test_tcgen05_hardware_equals_emulator(fa, fb, sat, d):
     assert r["mismatches"] == 0, (f"{r['mismatches']} of {r['cases']} words differ; first cases {r['first']}: "
                                   f"hardware {[hex(int(x)) for x in r['hardware'].reshape(-1)[r['first']]]} "
                                   f"emulator {[hex(int(x)) for x in r['emulator'].reshape(-1)[r['first']]]}")
+
+
+# ---- block-scaled kinds
+
+# (kind, A, B, scale, CUTLASS A type, B type, scale type)
+BS_CASES = [("mxf8f6f4", "e4m3", "e5m2", "ue8m0", "float_e4m3_t", "float_e5m2_t", "float_ue8m0_t"),
+            ("mxf8f6f4", "e2m3", "e2m1", "ue8m0", _E2M3, _E2M1, "float_ue8m0_t"),
+            ("mxf8f6f4", "e3m2", "e4m3", "ue8m0", _E3M2, "float_e4m3_t", "float_ue8m0_t"),
+            ("mxf4", "e2m1", "e2m1", "ue8m0", "float_e2m1_t", "float_e2m1_t", "float_ue8m0_t"),
+            ("mxf4nvf4-4x", "e2m1", "e2m1", "ue4m3", "float_e2m1_t", "float_e2m1_t", "float_ue4m3_t")]
+
+
+def test_block_scaled_descriptors_match_cutlass(tmp_path):
+    inc = _cutlass_include()
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if inc is None or not os.path.exists(nvcc):
+        pytest.skip("CUTLASS headers or nvcc not available")
+    lines = ["#include <cstdio>", "#include <cute/arch/mma_sm100_desc.hpp>",
+             "#include <cute/numeric/numeric_types.hpp>", "using namespace cute;", "int main() {"]
+    for *_, ta, tb, tsf in BS_CASES:
+        lines.append(f'  printf("%u\\n", uint32_t(UMMA::make_instr_desc_block_scaled<{ta}, {tb}, float, {tsf}, '
+                     f'128, 128, UMMA::Major::K, UMMA::Major::K>()));')
+    lines.append("  return 0; }")
+    src = tmp_path / "bs.cu"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "bs"
+    subprocess.run([nvcc, "-std=c++17", "-I", str(inc), "-o", str(exe), str(src)], check=True,
+                   capture_output=True, timeout=600)
+    want = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    got = [hwcheck.block_scaled_desc(kind, fa, fb, scale)[1] for kind, fa, fb, scale, *_ in BS_CASES]
+    assert got == want
+
+
+def test_block_scaled_shapes_and_validation():
+    with pytest.raises(ValueError):
+        hwcheck.block_scaled_desc("mxf4", "e4m3")
+    with pytest.raises(ValueError):
+        hwcheck.block_scaled_desc("mxf8f6f4", "e4m3", scale="ue4m3")
+    with pytest.raises(ValueError):
+        hwcheck.block_scaled_desc("mxf4nvf4-2x", "e2m1", scale="ue4m3")
+    a, b, c, sa, sb = hwcheck.random_block_scaled_tiles("mxf4nvf4-4x", "e2m1", None, 2, 0, "ue4m3")
+    assert (a.shape, b.shape, c.shape, sa.shape, sb.shape) == ((2, 128, 64), (2, 64, 128), (2, 128, 128),
+                                                               (2, 128, 4), (2, 128, 4))
+    assert int(sa.max()) <= 0x7F
+    assert hwcheck.block_scaled_rows(a.reshape(-1, 64), "e2m1", "mxf4").shape == (256, 32)
+    assert list(hwcheck.scale_words(np.array([[1, 2, 3, 4]]))) == [0x04030201]
+
+
+def test_abi_rejects_block_scaled_descriptors_outside_the_documented_encodings():
+    lib = nat.load()
+    fake = ctypes.c_void_p(1 << 20)
+    k8, d8 = hwcheck.block_scaled_desc("mxf8f6f4", "e4m3", "e2m1")
+    k4, d4 = hwcheck.block_scaled_desc("mxf4", "e2m1")
+    kn, dn = hwcheck.block_scaled_desc("mxf4nvf4-2x", "e2m1")
+    bad = [
+        (k8, d8 | (1 << 2)),                      # sparse
+        (k8, d8 | (1 << 4)),                      # B scale factor id 1
+        (k8, d8 | (1 << 29)),                     # A scale factor id 1
+        (k8, d8 | (1 << 31)),                     # K size bit
+        (k8, d8 | (1 << 15)),                     # A MN-major
+        (k8, d8 | (1 << 13)),                     # negate A
+        (k8, d8 & ~(1 << 23)),                    # UE4M3 scales on mxf8f6f4
+        (k8, (d8 & ~(0x3F << 17)) | (2 << 17)),   # N = 16
+        (k8, (d8 & ~(7 << 7)) | (2 << 7)),        # format code 2
+        (k4, (d4 & ~(7 << 7)) | (5 << 7)),        # f8f6f4 E2M1 code on mxf4
+        (k4, d4 & ~(1 << 23)),                    # UE4M3 on mxf4
+        (kn, dn & ~(1 << 23)),                    # UE4M3 on the two-scale mxf4nvf4
+        (9, d4),                                  # unknown kind
+    ]
+    for kind, desc in bad:
+        rc = lib.t5e_tcgen05_block_scaled_tiles(kind, desc, fake, fake, fake, fake, fake, fake, 1, fake, None)
+        assert rc == nat.ERR_INVALID, (kind, hex(desc), rc)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("kind,fa,fb,scale", hwcheck.BS_PAIRS,
+                         ids=[f"{p[0]}-{p[1]}x{p[2]}-{p[3]}" for p in hwcheck.BS_PAIRS])
+def test_tcgen05_block_scaled_hardware_equals_emulator(kind, fa, fb, scale):
+    a, b, c, sa, sb = hwcheck.random_block_scaled_tiles(kind, fa, fb, 4, 23, scale)
+    r = hwcheck.cross_check_block_scaled(a, b, c, sa, sb, kind, fa, fb, scale)
+    assert r["mismatches"] == 0, (f"{r['mismatches']} of {r['cases']} words differ; first cases {r['first']}: "
+                                  f"hardware {[hex(int(x)) for x in r['hardware'].reshape(-1)[r['first']]]} "
+                                  f"emulator {[hex(int(x)) for x in r['emulator'].reshape(-1)[r['first']]]}")
