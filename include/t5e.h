@@ -173,6 +173,21 @@ int t5e_mma_dot_batch(const t5e_model* model, const t5e_batch* batch, void* stre
  * used to cross-check the specialised kernels on the device. */
 int t5e_mma_dot_batch_generic(const t5e_model* model, const t5e_batch* batch, void* stream);
 
+/* The same evaluation for a batch held in host memory (pinned for the copies
+ * to overlap), streamed through device buffers the caller provides: `host`
+ * and `dev` describe the same plain batch (tile_m = tile_n = 1), with host and
+ * device pointers.  The cases are cut into chunks of `chunk_cases` (0: a
+ * quarter of the batch; rounded up to whole 1024-case groups).  Each chunk's
+ * operands are copied up on a library-owned stream, evaluated on `stream`
+ * once they have landed, and its D words (and status bytes, when both
+ * batches carry a status array) copied down on another library-owned stream.
+ * The uploads first wait for the work already queued on `stream`.  Returns
+ * when every result word is in host memory.  No counterpart in the reference:
+ * it stands for the host-side loop that hands cases to the model and
+ * collects the words.  Allocates no memory. */
+int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
+                             uint64_t chunk_cases, void* stream);
+
 /* Device-side packing: words [rows][k] (raw uint32 container words, the
  * reference's operand convention) -> packed rows of out_stride bytes each
  * (padding bits are zero). */

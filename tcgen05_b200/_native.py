@@ -110,6 +110,7 @@ EXPORTED = (
     "t5e_last_error",
     "t5e_mma_dot_batch",
     "t5e_mma_dot_batch_generic",
+    "t5e_mma_dot_batch_staged",
     "t5e_pack_rows",
     "t5e_sparse_active",
     "t5e_tcgen05_tiles",
@@ -148,6 +149,9 @@ def load() -> ctypes.CDLL:
     lib.t5e_sparse_active.restype = ctypes.c_int
     lib.t5e_sparse_active.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_void_p, ctypes.c_int32,
                                       ctypes.c_int32, ctypes.c_void_p]
+    lib.t5e_mma_dot_batch_staged.restype = ctypes.c_int
+    lib.t5e_mma_dot_batch_staged.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
+                                             ctypes.c_void_p]
     lib.t5e_tcgen05_tiles.restype = ctypes.c_int
     lib.t5e_tcgen05_tiles.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,

@@ -5,6 +5,8 @@
 
 #include <cstdio>
 #include <cstring>
+#include <mutex>
+#include <vector>
 
 #include "t5e.h"
 #include "t5e_dispatch.h"
@@ -176,6 +178,42 @@ int validate(const t5e_model* M, const t5e_batch* B) {
   return T5E_OK;
 }
 
+// Upload and download streams of a device for t5e_mma_dot_batch_staged,
+// created on first use and kept for the life of the process.
+struct CopyStreams {
+  cudaStream_t up = nullptr, down = nullptr;
+};
+CopyStreams g_copy_streams[64];
+std::mutex g_copy_mutex;
+
+int copy_streams(int dev, CopyStreams& out) {
+  if (dev < 0 || dev >= 64) return T5E_ERR_INVALID;
+  std::lock_guard<std::mutex> lock(g_copy_mutex);
+  CopyStreams& s = g_copy_streams[dev];
+  if (!s.up) {
+    cudaStream_t up = nullptr, down = nullptr;
+    cudaError_t e = cudaStreamCreateWithFlags(&up, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&down, cudaStreamNonBlocking);
+    if (e != cudaSuccess) {
+      if (up) cudaStreamDestroy(up);
+      set_cuda_error("copy stream", e);
+      return T5E_ERR_CUDA;
+    }
+    s.up = up;
+    s.down = down;
+  }
+  out = s;
+  return T5E_OK;
+}
+
+// The host and device descriptions of a staged batch describe the same plain
+// (untiled) batch.
+bool same_geometry(const t5e_batch& h, const t5e_batch& d) {
+  return h.n == d.n && h.k == d.k && h.flags == d.flags && h.sparse == d.sparse && h.meta_words == d.meta_words &&
+         h.a_stride == d.a_stride && h.b_stride == d.b_stride && h.c_bytes == d.c_bytes && h.nscale == d.nscale &&
+         h.tile_m == 1 && h.tile_n == 1 && d.tile_m == 1 && d.tile_n == 1;
+}
+
 }  // namespace t5e
 
 using namespace t5e;
@@ -200,6 +238,111 @@ int t5e_mma_dot_batch(const t5e_model* model, const t5e_batch* batch, void* stre
   const int fast = launch_fast(*model, *batch, static_cast<cudaStream_t>(stream));
   if (fast != T5E_ERR_UNSUPPORTED) return fast;
   return t5e_mma_dot_batch_generic(model, batch, stream);
+}
+
+int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
+                             uint64_t chunk_cases, void* stream) {
+  if (!host || !dev) return T5E_ERR_INVALID;
+  const int v = validate(model, dev);
+  if (v != T5E_OK) return v;
+  if (!same_geometry(*host, *dev)) return T5E_ERR_INVALID;
+  const uint64_t n = dev->n;
+  if (n == 0) return T5E_OK;
+  if (!host->a || !host->b || !host->c || !host->d) return T5E_ERR_INVALID;
+  if (host->nscale > 0 && (!host->scale_a || !host->scale_b)) return T5E_ERR_INVALID;
+  if (host->sparse != 0 && !host->metadata) return T5E_ERR_INVALID;
+  const bool with_status = host->status && dev->status;
+  const bool broadcast = host->sparse != 0 && (host->flags & T5E_META_BROADCAST);
+  int devid = 0;
+  cudaError_t e = cudaGetDevice(&devid);
+  if (e != cudaSuccess) {
+    set_cuda_error("cudaGetDevice", e);
+    return T5E_ERR_CUDA;
+  }
+  CopyStreams cs;
+  const int rc_streams = copy_streams(devid, cs);
+  if (rc_streams != T5E_OK) return rc_streams;
+  cudaStream_t comp = static_cast<cudaStream_t>(stream);
+  // chunks of whole 1024-case groups keep every chunk's rows 16-byte aligned
+  uint64_t step = chunk_cases ? chunk_cases : (n + 3) / 4;
+  step = (step + 1023) / 1024 * 1024;
+  const uint64_t chunks = (n + step - 1) / step;
+  std::vector<cudaEvent_t> ev;
+  ev.reserve(2 * chunks + 1);
+  auto event = [&](cudaEvent_t& out) {
+    const cudaError_t err = cudaEventCreateWithFlags(&out, cudaEventDisableTiming);
+    if (err == cudaSuccess) ev.push_back(out);
+    return err;
+  };
+  auto h2d = [&](const void* hbase, void* dbase, uint64_t offset, uint64_t bytes) {
+    return cudaMemcpyAsync(static_cast<uint8_t*>(dbase) + offset, static_cast<const uint8_t*>(hbase) + offset, bytes,
+                           cudaMemcpyHostToDevice, cs.up);
+  };
+  int rc = T5E_OK;
+  cudaEvent_t start = nullptr;
+  // the uploads wait for work already queued on the caller's stream, which
+  // may still read the device buffers about to be overwritten
+  e = event(start);
+  if (e == cudaSuccess) e = cudaEventRecord(start, comp);
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs.up, start, 0);
+  if (e == cudaSuccess && broadcast)
+    e = h2d(host->metadata, const_cast<uint32_t*>(dev->metadata), 0, (uint64_t)dev->meta_words * 4);
+  for (uint64_t c = 0; c < chunks && e == cudaSuccess && rc == T5E_OK; ++c) {
+    const uint64_t s0 = c * step, m = (s0 + step < n ? s0 + step : n) - s0;
+    e = h2d(host->a, const_cast<void*>(dev->a), s0 * (uint64_t)dev->a_stride, m * (uint64_t)dev->a_stride);
+    if (e == cudaSuccess)
+      e = h2d(host->b, const_cast<void*>(dev->b), s0 * (uint64_t)dev->b_stride, m * (uint64_t)dev->b_stride);
+    if (e == cudaSuccess)
+      e = h2d(host->c, const_cast<void*>(dev->c), s0 * (uint64_t)dev->c_bytes, m * (uint64_t)dev->c_bytes);
+    if (e == cudaSuccess && dev->nscale > 0) {
+      e = h2d(host->scale_a, const_cast<uint8_t*>(dev->scale_a), s0 * (uint64_t)dev->nscale, m * (uint64_t)dev->nscale);
+      if (e == cudaSuccess)
+        e = h2d(host->scale_b, const_cast<uint8_t*>(dev->scale_b), s0 * (uint64_t)dev->nscale,
+                m * (uint64_t)dev->nscale);
+    }
+    if (e == cudaSuccess && dev->sparse != 0 && !broadcast)
+      e = h2d(host->metadata, const_cast<uint32_t*>(dev->metadata), s0 * 4 * (uint64_t)dev->meta_words,
+              m * 4 * (uint64_t)dev->meta_words);
+    cudaEvent_t landed = nullptr, done = nullptr;
+    if (e == cudaSuccess) e = event(landed);
+    if (e == cudaSuccess) e = cudaEventRecord(landed, cs.up);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(comp, landed, 0);
+    if (e != cudaSuccess) break;
+    t5e_batch sub = *dev;
+    sub.n = m;
+    sub.a = static_cast<const uint8_t*>(dev->a) + s0 * (uint64_t)dev->a_stride;
+    sub.b = static_cast<const uint8_t*>(dev->b) + s0 * (uint64_t)dev->b_stride;
+    sub.c = static_cast<const uint8_t*>(dev->c) + s0 * (uint64_t)dev->c_bytes;
+    sub.d = dev->d + s0;
+    sub.status = dev->status ? dev->status + s0 : nullptr;
+    if (dev->nscale > 0) {
+      sub.scale_a = dev->scale_a + s0 * (uint64_t)dev->nscale;
+      sub.scale_b = dev->scale_b + s0 * (uint64_t)dev->nscale;
+    }
+    if (dev->sparse != 0 && !broadcast) sub.metadata = dev->metadata + s0 * (uint64_t)dev->meta_words;
+    rc = t5e_mma_dot_batch(model, &sub, stream);
+    if (rc != T5E_OK) break;
+    e = event(done);
+    if (e == cudaSuccess) e = cudaEventRecord(done, comp);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(cs.down, done, 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(host->d + s0, dev->d + s0, m * 4, cudaMemcpyDeviceToHost, cs.down);
+    if (e == cudaSuccess && with_status)
+      e = cudaMemcpyAsync(host->status + s0, dev->status + s0, m, cudaMemcpyDeviceToHost, cs.down);
+  }
+  if (e != cudaSuccess) {
+    set_cuda_error("t5e_mma_dot_batch_staged copy", e);
+    rc = T5E_ERR_CUDA;
+  }
+  // every copy and kernel this call queued has finished when it returns
+  const cudaError_t e_up = cudaStreamSynchronize(cs.up);
+  const cudaError_t e_down = cudaStreamSynchronize(cs.down);
+  if (rc == T5E_OK && (e_up != cudaSuccess || e_down != cudaSuccess)) {
+    set_cuda_error("t5e_mma_dot_batch_staged synchronize", e_up != cudaSuccess ? e_up : e_down);
+    rc = T5E_ERR_CUDA;
+  }
+  for (cudaEvent_t x : ev) cudaEventDestroy(x);
+  return rc;
 }
 
 int t5e_pack_rows(int32_t format, const uint32_t* words, uint64_t rows, int32_t k, void* out, int64_t out_stride,

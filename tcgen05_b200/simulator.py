@@ -458,14 +458,12 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
     cut into chunks; each chunk's operands are copied to the device on one
     stream, evaluated on the current stream once its copy has landed, and its
     result words (and status bytes) copied back on a third stream, so the
-    copies in both directions overlap each other and the kernels."""
+    copies in both directions overlap each other and the kernels.  The
+    library's t5e_mma_dot_batch_staged runs that loop; the loop below it
+    serves the generic kernel and metadata shared by every case."""
     import torch
 
     comp = torch.cuda.current_stream(dev)
-    up, down = _copy_streams(dev)
-    # the device buffers below come from the allocator on the current stream:
-    # the uploads wait for whatever that stream still has queued
-    up.wait_stream(comp)
     # per-case status bytes only exist for sparse selections: every other
     # per-case error (scale cover, K range) is decided for the whole batch on
     # the host before the launch
@@ -490,6 +488,32 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
     step = (step + 1023) // 1024 * 1024
     sa_h = None if sa is None else sa.view(torch.uint8)
     sb_h = None if sb is None else sb.view(torch.uint8)
+    a_flags = flags | (nat.FLAG_SPARSE_A_COMPRESSED if a.compressed else 0)
+    if not generic and (meta is None or per_case_meta):
+        # the chunk loop runs inside the library: one call streams the whole
+        # batch (copies up, kernels, copies down) and returns with `out` filled
+        db = runtime.DeviceBatch(n=n, k=k, a=a_dev, b=b_dev, c=c_dev, sparse=sparse, flags=a_flags)
+        hb = runtime.DeviceBatch(n=n, k=k, a=a.data, b=b.data, c=c, sparse=sparse, flags=a_flags)
+        if sa_dev is not None:
+            db.scale_a, db.scale_b = sa_dev, sb_dev
+            hb.scale_a, hb.scale_b = sa_h, sb_h
+        if meta_dev is not None:
+            db.metadata = meta_dev
+            hb.metadata = meta.view(torch.int32)
+        dev_struct = runtime.make_batch_struct(db, d_dev, st_dev)
+        host_struct = runtime.make_batch_struct(hb, out, st_host)
+        nat.check(lib.t5e_mma_dot_batch_staged(ctypes.byref(desc), ctypes.byref(host_struct), ctypes.byref(dev_struct),
+                                               step, handle), "t5e_mma_dot_batch_staged")
+        if check:
+            st_np = st_host.numpy()
+            if st_np.any():
+                first = int(np.flatnonzero(st_np)[0])
+                _raise_case_status(selected, int(st_np[first]), meta_message=lambda: meta_error(first))
+        return out
+    up, down = _copy_streams(dev)
+    # the device buffers above come from the allocator on the current stream:
+    # the uploads wait for whatever that stream still has queued
+    up.wait_stream(comp)
     for s0 in range(0, n, step):
         s1 = min(n, s0 + step)
         with torch.cuda.stream(up):
@@ -505,7 +529,7 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
             landed.record(up)
         comp.wait_event(landed)
         db = runtime.DeviceBatch(n=s1 - s0, k=k, a=a_dev[s0:s1], b=b_dev[s0:s1], c=c_dev[s0:s1], sparse=sparse,
-                                 flags=flags | (nat.FLAG_SPARSE_A_COMPRESSED if a.compressed else 0))
+                                 flags=a_flags)
         if sa_dev is not None:
             db.scale_a, db.scale_b = sa_dev[s0:s1], sb_dev[s0:s1]
         if meta_dev is not None:
