@@ -184,7 +184,8 @@ int t5e_mma_dot_batch_generic(const t5e_model* model, const t5e_batch* batch, vo
  * The uploads first wait for the work already queued on `stream`.  Returns
  * when every result word is in host memory.  No counterpart in the reference:
  * it stands for the host-side loop that hands cases to the model and
- * collects the words.  Allocates no memory. */
+ * collects the words.  Allocates no device memory (it creates CUDA events,
+ * released before it returns). */
 int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
                              uint64_t chunk_cases, void* stream);
 

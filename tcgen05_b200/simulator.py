@@ -491,7 +491,8 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
     a_flags = flags | (nat.FLAG_SPARSE_A_COMPRESSED if a.compressed else 0)
     if not generic and (meta is None or per_case_meta):
         # the chunk loop runs inside the library: one call streams the whole
-        # batch (copies up, kernels, copies down) and returns with `out` filled
+        # batch (copies up, kernels, copies down) through the device buffers
+        # above and returns with `out` filled
         db = runtime.DeviceBatch(n=n, k=k, a=a_dev, b=b_dev, c=c_dev, sparse=sparse, flags=a_flags)
         hb = runtime.DeviceBatch(n=n, k=k, a=a.data, b=b.data, c=c, sparse=sparse, flags=a_flags)
         if sa_dev is not None:
