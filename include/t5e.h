@@ -189,6 +189,27 @@ int t5e_mma_dot_batch_generic(const t5e_model* model, const t5e_batch* batch, vo
 int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
                              uint64_t chunk_cases, void* stream);
 
+/* Size of the device array that t5e_mma_dot_batch_noalloc stages batches in. */
+#define T5E_NOALLOC_STAGE_BYTES (32u * 1024u * 1024u)
+
+/* The evaluation of a plain batch (tile_m = tile_n = 1) held in host memory,
+ * for callers that may not allocate GPU memory: a plugin whose host
+ * application owns every device memory pool, a loop that must not allocate
+ * once it runs, a process held to a fixed memory budget.  No counterpart in
+ * the reference.  `host` holds host pointers only.  The operands, C words,
+ * scales and metadata are copied on `stream` into one static device array of
+ * T5E_NOALLOC_STAGE_BYTES that every GPU loading the library holds until the
+ * process exits; the result region is cleared, the batch evaluated as by
+ * t5e_mma_dot_batch, and the D words (and status bytes) copied back.  Returns
+ * when they are in host memory.  A batch whose regions (each rounded up to
+ * 256 bytes) do not fit in the array is rejected with T5E_ERR_INVALID and a
+ * message in t5e_last_error().  Calls no allocator.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress, with
+ * that device current); make it before any stream capture.  Every call on a
+ * device shares the one array: calls that overlap in time on that device, on
+ * any streams or host threads, overwrite each other's data. */
+int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch* host, void* stream);
+
 /* Device-side packing: words [rows][k] (raw uint32 container words, the
  * reference's operand convention) -> packed rows of out_stride bytes each
  * (padding bits are zero). */

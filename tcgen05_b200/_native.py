@@ -50,6 +50,8 @@ ERR_UNSUPPORTED = -2
 ERR_CUDA = -3
 ERR_K_RANGE = -4
 MAX_K = 65536
+# bytes of the static device array t5e_mma_dot_batch_noalloc stages batches in
+NOALLOC_STAGE_BYTES = 32 * 1024 * 1024
 
 CASE_OK, CASE_BAD_SELECTOR, CASE_EMPTY, CASE_SCALE_COVER, CASE_META_WORDS, CASE_TIMEOUT = 0, 1, 2, 3, 4, 5
 
@@ -111,6 +113,7 @@ EXPORTED = (
     "t5e_mma_dot_batch",
     "t5e_mma_dot_batch_generic",
     "t5e_mma_dot_batch_staged",
+    "t5e_mma_dot_batch_noalloc",
     "t5e_pack_rows",
     "t5e_sparse_active",
     "t5e_tcgen05_tiles",
@@ -152,6 +155,8 @@ def load() -> ctypes.CDLL:
     lib.t5e_mma_dot_batch_staged.restype = ctypes.c_int
     lib.t5e_mma_dot_batch_staged.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                              ctypes.c_void_p]
+    lib.t5e_mma_dot_batch_noalloc.restype = ctypes.c_int
+    lib.t5e_mma_dot_batch_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.t5e_tcgen05_tiles.restype = ctypes.c_int
     lib.t5e_tcgen05_tiles.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,

@@ -32,6 +32,10 @@ void set_cuda_error(const char* what, cudaError_t err);
 // Grid size for a grid-stride loop over n items.
 int grid_for(uint64_t n, int block);
 
+// The host-side checks of t5e_mma_dot_batch (T5E_OK or the error code it
+// would return), made without any CUDA call.
+int validate(const t5e_model* M, const t5e_batch* B);
+
 // Raises Kernel's dynamic shared-memory limit to `bytes` on the current
 // device, once per device and kernel (one flag array per kernel; host
 // threads may race to set it, which is harmless: the attribute value is the
