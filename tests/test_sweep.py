@@ -139,3 +139,43 @@ def test_gpu_sweep_every_path_matches_generic_and_oracle():
     for i in range(4):
         s = (int(halves[0]["results"][i]["checksum"], 16) + int(halves[1]["results"][i]["checksum"], 16))
         assert s == int(whole["results"][i]["checksum"], 16)
+
+
+def _host_cases_from_device(spec, g):
+    """Device-generated cases copied to host memory in the oracle's form."""
+    def words(x):
+        if x is None:
+            return None
+        return torch.where(x >= 1 << 31, x - (1 << 32), x).to(torch.int32).cpu().numpy().view(np.uint32)
+
+    def scales(x):
+        return None if x is None else x.to(torch.uint8).cpu().numpy()
+
+    return workloads.Cases(spec.descriptor, words(g["a"]), words(g["b"]), words(g["c"]), scales(g["scale_a"]),
+                           scales(g["scale_b"]), words(g["meta"]), name=spec.name)
+
+
+@pytest.mark.gpu
+def test_gpu_every_path_at_full_size_matches_oracle():
+    """Every path of the sweep at its full size (1M cases each, 46M in all):
+    each device word equals the oracle's word for the same case.  The cases
+    come from the device generator (the numpy mirror is checked above) and
+    are copied to the host for the oracle."""
+    from oracle import oracle
+
+    dev = torch.device("cuda", 0)
+    total, chunk = 1_000_000, 1 << 18
+    bad = {}
+    checked = 0
+    for spec in PATHS:
+        for lo in range(0, total, chunk):
+            count = min(chunk, total - lo)
+            g = sweep.generate(spec, lo, count, total, torch, dev)
+            got = sweep._device_eval(spec, g, dev, generic=False).cpu().numpy().astype(np.uint32)
+            want = oracle.eval_cases(_host_cases_from_device(spec, g))
+            diff = np.flatnonzero(got != want)
+            if diff.size:
+                bad.setdefault(spec.name, []).append((lo + int(diff[0]), int(diff.size)))
+            checked += count
+    assert checked == total * len(PATHS)
+    assert not bad, bad
