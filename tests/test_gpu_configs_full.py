@@ -6,17 +6,16 @@ to container words and evaluated by the oracle on every host core.
 Sizes: TF32 K=8 65,536 cases; E4M3 x E5M2 K=32 2^20 cases with F32 D and
 with F16 D; MXF8F6F4 E2M3 x E3M2 2^22; U8 x S8 2^22 saturating and
 wrapping; NVFP4 K=64 2^24 dense and 2^24 pairwise-sparse (logical K=128,
-compressed A rows)."""
+compressed A rows); the BF16 matrix configuration, 4096 tiles of
+M=128 x N=256 x K=16 (134M cases), expanded tile by tile to one row pair per
+case for the oracle."""
 
 from __future__ import annotations
-
-import ctypes
 
 import numpy as np
 import pytest
 
 from oracle import oracle
-from tcgen05_b200 import _native as nat
 from tcgen05_b200 import make_model, packing, runtime, workloads
 
 pytestmark = pytest.mark.gpu
@@ -83,3 +82,34 @@ def test_configuration_at_full_size_matches_oracle(name):
             first = (lo + int(diff[0]), int(got[lo + diff[0]]), int(want[diff[0]]))
         mismatches += int(diff.size)
     assert mismatches == 0, f"{name}: {mismatches} words differ, first (case, device, oracle) = {first}"
+
+
+def test_matrix_configuration_at_full_size_matches_oracle():
+    import torch
+
+    dev = torch.device("cuda", 0)
+    model, db = workloads.device_config("matrix-bf16", dev, seed=0)
+    desc = model.descriptor()
+    tm, tn = db.tile_m, db.tile_n
+    tiles = db.n // (tm * tn)
+    assert tiles == 4096
+    d, _ = runtime.launch(desc, db, status=False)
+    got = _host(d).view(np.uint32)
+    per_call = 32  # tiles per oracle call
+    mismatches, first = 0, None
+    for t0 in range(0, tiles, per_call):
+        t1 = min(tiles, t0 + per_call)
+        a_rows = packing.unpack_rows(_host(db.a[t0 * tm:t1 * tm]), desc.a_format, db.k).reshape(t1 - t0, tm, db.k)
+        b_rows = packing.unpack_rows(_host(db.b[t0 * tn:t1 * tn]), desc.b_format, db.k).reshape(t1 - t0, tn, db.k)
+        # case (row, col) of a tile pairs A row `row` with B row `col`
+        a = np.repeat(a_rows, tn, axis=1).reshape(-1, db.k)
+        b = np.tile(b_rows, (1, tm, 1)).reshape(-1, db.k)
+        lo, hi = t0 * tm * tn, t1 * tm * tn
+        c = _host(db.c[lo:hi]).view(np.uint32)
+        want, ost = oracle.mma_dot_batch(a, b, c, a_format="bf16")
+        assert not ost.any()
+        diff = np.flatnonzero(got[lo:hi] != want)
+        if diff.size and first is None:
+            first = (lo + int(diff[0]), int(got[lo + diff[0]]), int(want[diff[0]]))
+        mismatches += int(diff.size)
+    assert mismatches == 0, f"matrix-bf16: {mismatches} words differ, first (case, device, oracle) = {first}"
