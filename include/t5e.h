@@ -210,6 +210,16 @@ int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, cons
  * any streams or host threads, overwrite each other's data. */
 int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch* host, void* stream);
 
+/* Integer issue-rate probe, a measurement helper for the integer roofline
+ * (no counterpart in the reference).  Launches on `stream` two blocks of 1024
+ * threads per SM that issue nothing but independent chains of one pipe's
+ * instructions: pipe 0 the ALU pipe (LOP3, SHF), pipe 1 the FMA pipe (IMAD);
+ * `iters` (1..2^20) loop iterations of 256 such instructions per
+ * thread.  Stores the number of those warp instructions the launch issues in
+ * *warp_instructions; timed with events on `stream`, it gives the pipe's
+ * issue rate at the SM clock of the moment. */
+int t5e_issue_probe(int32_t pipe, uint32_t iters, uint64_t* warp_instructions, void* stream);
+
 /* Device-side packing: words [rows][k] (raw uint32 container words, the
  * reference's operand convention) -> packed rows of out_stride bytes each
  * (padding bits are zero). */

@@ -114,6 +114,7 @@ EXPORTED = (
     "t5e_mma_dot_batch_generic",
     "t5e_mma_dot_batch_staged",
     "t5e_mma_dot_batch_noalloc",
+    "t5e_issue_probe",
     "t5e_pack_rows",
     "t5e_sparse_active",
     "t5e_tcgen05_tiles",
@@ -157,6 +158,8 @@ def load() -> ctypes.CDLL:
                                              ctypes.c_void_p]
     lib.t5e_mma_dot_batch_noalloc.restype = ctypes.c_int
     lib.t5e_mma_dot_batch_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.t5e_issue_probe.restype = ctypes.c_int
+    lib.t5e_issue_probe.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint64), ctypes.c_void_p]
     lib.t5e_tcgen05_tiles.restype = ctypes.c_int
     lib.t5e_tcgen05_tiles.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_void_p,
                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,

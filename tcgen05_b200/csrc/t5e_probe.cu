@@ -1,0 +1,93 @@
+// t5e_probe.cu -- issue-rate probes for the integer roofline.
+//
+// The emulator kernels are integer work on the ALU pipe (LOP3, SHF, PRMT,
+// IMNMX, ...) and the FMA pipe (IMAD, IMUL; the assembler also issues 32-bit
+// adds there), not tensor-core work, so their
+// compute roofline is the issue rate of those pipes at the SM clock the GPU
+// runs at.  No vendor figure states it for this part, so it is measured:
+// these kernels issue nothing but independent chains of one pipe's
+// instructions, a known number per launch, at full occupancy (two blocks of
+// 1024 threads per SM).  The caller times a launch with events and divides.
+//
+// Each step computes eight new chain values from the eight previous ones
+// (chain c reads chains c, c+1 and c+3), so every result feeds three later
+// instructions: the assembler can neither drop nor fuse them, and eight
+// instructions of a warp are independent at every step.
+#include <cuda_runtime.h>
+
+#include "t5e.h"
+#include "t5e_dispatch.h"
+
+namespace t5e {
+namespace probe {
+
+constexpr int kThreads = 1024;
+constexpr int kBlocksPerSm = 2;
+constexpr int kChains = 8;
+constexpr int kSteps = 32;  // steps per loop iteration
+constexpr uint32_t kMaxIters = 1u << 20;
+
+// never written in practice: a store that depends on every chain keeps the
+// chains live
+__device__ uint32_t g_sink[1024];
+
+template <int PIPE>
+__global__ void __launch_bounds__(kThreads, kBlocksPerSm) issue_kernel(uint32_t iters, uint32_t seed) {
+  uint32_t x[kChains];
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) x[c] = (seed + 0x9E3779B9u * (uint32_t)(c + 1)) ^ (threadIdx.x * 0x85EBCA6Bu) ^ blockIdx.x;
+  for (uint32_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int s = 0; s < kSteps; ++s) {
+      uint32_t y[kChains];
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) {
+        const uint32_t p = x[(c + 1) % kChains], q = x[(c + 3) % kChains];
+        if constexpr (PIPE == 0) {
+          // ALU pipe: LOP3 and SHF in turn (32-bit adds are left out: the
+          // assembler may issue them on the FMA pipe)
+          if (c % 2 == 0) {
+            asm volatile("lop3.b32 %0, %1, %2, %3, 0x96;" : "=r"(y[c]) : "r"(x[c]), "r"(p), "r"(q));
+          } else {
+            asm volatile("shf.l.wrap.b32 %0, %1, %2, %3;" : "=r"(y[c]) : "r"(x[c]), "r"(p), "r"(q));
+          }
+        } else {
+          // FMA pipe: IMAD
+          asm volatile("mad.lo.u32 %0, %1, %2, %3;" : "=r"(y[c]) : "r"(x[c]), "r"(p), "r"(q));
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) x[c] = y[c];
+    }
+  }
+  uint32_t acc = 0;
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) acc ^= x[c];
+  if (acc == 0x2545F491u && seed == 0x68E31DA4u) g_sink[blockIdx.x & 1023u] = acc;
+}
+
+}  // namespace probe
+}  // namespace t5e
+
+using namespace t5e;
+
+extern "C" int t5e_issue_probe(int32_t pipe, uint32_t iters, uint64_t* warp_instructions, void* stream) {
+  using namespace t5e::probe;
+  if ((pipe != 0 && pipe != 1) || iters < 1 || iters > kMaxIters || !warp_instructions) return T5E_ERR_INVALID;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) {
+    set_cuda_error("t5e_issue_probe: device attributes", e);
+    return T5E_ERR_CUDA;
+  }
+  const int grid = sms * kBlocksPerSm;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // the mix of the ALU probe: in each step, even chains LOP3, odd chains SHF
+  if (pipe == 0) issue_kernel<0><<<grid, kThreads, 0, s>>>(iters, 0x1234567u);
+  else issue_kernel<1><<<grid, kThreads, 0, s>>>(iters, 0x1234567u);
+  const int rc = kernel_status("t5e_issue_probe launch");
+  if (rc != T5E_OK) return rc;
+  *warp_instructions = (uint64_t)grid * (kThreads / 32) * iters * kSteps * kChains;
+  return T5E_OK;
+}
