@@ -280,18 +280,27 @@ def run_ours(args) -> int:
         host.append((item, pa, pb, pc, out))
         h2d += pa.numel() + pb.numel() + pc.numel() * pc.element_size()
         d2h += out.numel() * 4  # result words (dense batches carry no per-case status bytes)
-    for _ in range(2):
-        for item, pa, pb, pc, out in host:
-            t5.mma_dot_batch(t5.PackedRows(pa, K_ELEMS), t5.PackedRows(pb, K_ELEMS), pc, model=item["model"],
-                             out=out)
+    def e2e_run(steps, depth=4):
+        # every call returns once its copies and kernels are queued (wait=False), so each batch's upload
+        # follows the previous one on the link; at most `depth` calls are in flight, so the device buffers
+        # they stream through come back to the allocator; every result word is in host memory when the
+        # last wait returns
+        pending = []
+        for _ in range(steps):
+            for item, pa, pb, pc, out in host:
+                pending.append(t5.mma_dot_batch(t5.PackedRows(pa, K_ELEMS), t5.PackedRows(pb, K_ELEMS), pc,
+                                                model=item["model"], out=out, wait=False))
+                if len(pending) > depth:
+                    pending.pop(0).wait()
+        for p in pending:
+            p.wait()
+
+    e2e_run(e2e_steps)  # the same calls once untimed: the allocator then holds every buffer the timed run needs
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
     t0 = time.perf_counter()
-    for _ in range(e2e_steps):
-        for item, pa, pb, pc, out in host:
-            t5.mma_dot_batch(t5.PackedRows(pa, K_ELEMS), t5.PackedRows(pb, K_ELEMS), pc, model=item["model"],
-                             out=out)
+    e2e_run(e2e_steps)
     torch.cuda.synchronize(device)
     e2e_s = time.perf_counter() - t0
     ok_e2e = all(np.array_equal(out.numpy(), item["d"].cpu().numpy()) for item, _, _, _, out in host)
@@ -361,7 +370,9 @@ def run_ours(args) -> int:
                          "int_pipe": int_pipe,
                          "binds": max(fracs, key=fracs.get)},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "steps": e2e_steps},
+                    "steps": e2e_steps,
+                    "calls": "mma_dot_batch(pinned PackedRows, pinned out, wait=False) per batch, every wait "
+                             "inside the timed region"},
             "clocks": clocks,
         }
         if world == 1 and not args.no_configs:

@@ -189,6 +189,21 @@ int t5e_mma_dot_batch_generic(const t5e_model* model, const t5e_batch* batch, vo
 int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
                              uint64_t chunk_cases, void* stream);
 
+/* The same streaming evaluation, returning once every copy and kernel is
+ * queued (no counterpart in the reference: it lets a caller keep several host
+ * batches in flight).  `done_event` is a cudaEvent_t the caller created on
+ * the current device; it is recorded after the last download, so waiting on
+ * it (cudaEventSynchronize, or cudaStreamWaitEvent before work that reads the
+ * words) marks the moment every result word is in host memory.  Until then
+ * the host and device buffers must stay untouched.  The uploads still wait
+ * for work already queued on `stream`, but `stream` does not wait for the
+ * downloads: the next call's uploads queue right behind this call's, on the
+ * same library-owned upload stream, so back-to-back calls keep the
+ * host-to-device link busy.  An empty batch queues nothing and records the
+ * event on `stream`.  On an error return, everything queued has finished. */
+int t5e_mma_dot_batch_staged_async(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
+                                   uint64_t chunk_cases, void* stream, void* done_event);
+
 /* Size of the device array that t5e_mma_dot_batch_noalloc stages batches in. */
 #define T5E_NOALLOC_STAGE_BYTES (32u * 1024u * 1024u)
 

@@ -20,11 +20,12 @@ from .model import (
     make_model,
     normalize_format,
 )
-from .simulator import PackedRows, mma, mma_batch, mma_dot, mma_dot_batch, sparse_active_indices
+from .simulator import PackedRows, PendingBatch, mma, mma_batch, mma_dot, mma_dot_batch, sparse_active_indices
 
 __all__ = [
     "DotProduct",
     "PackedRows",
+    "PendingBatch",
     "ScalarModel",
     "Tcgen05BlockScaledMmaModel",
     "Tcgen05I8S32MmaModel",

@@ -113,6 +113,7 @@ EXPORTED = (
     "t5e_mma_dot_batch",
     "t5e_mma_dot_batch_generic",
     "t5e_mma_dot_batch_staged",
+    "t5e_mma_dot_batch_staged_async",
     "t5e_mma_dot_batch_noalloc",
     "t5e_issue_probe",
     "t5e_pack_rows",
@@ -156,6 +157,9 @@ def load() -> ctypes.CDLL:
     lib.t5e_mma_dot_batch_staged.restype = ctypes.c_int
     lib.t5e_mma_dot_batch_staged.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_uint64,
                                              ctypes.c_void_p]
+    lib.t5e_mma_dot_batch_staged_async.restype = ctypes.c_int
+    lib.t5e_mma_dot_batch_staged_async.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                                   ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
     lib.t5e_mma_dot_batch_noalloc.restype = ctypes.c_int
     lib.t5e_mma_dot_batch_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
     lib.t5e_issue_probe.restype = ctypes.c_int

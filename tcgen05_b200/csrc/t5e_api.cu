@@ -240,14 +240,30 @@ int t5e_mma_dot_batch(const t5e_model* model, const t5e_batch* batch, void* stre
   return t5e_mma_dot_batch_generic(model, batch, stream);
 }
 
-int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
-                             uint64_t chunk_cases, void* stream) {
+}  // extern "C"
+
+namespace t5e {
+
+// The chunked upload / evaluate / download loop behind both staged entry
+// points.  With done_event null it returns once every result word is in host
+// memory; otherwise it returns once everything is queued and records
+// done_event on the download stream after the last download.
+int staged_run(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev, uint64_t chunk_cases,
+               void* stream, cudaEvent_t done_event) {
   if (!host || !dev) return T5E_ERR_INVALID;
   const int v = validate(model, dev);
   if (v != T5E_OK) return v;
   if (!same_geometry(*host, *dev)) return T5E_ERR_INVALID;
   const uint64_t n = dev->n;
-  if (n == 0) return T5E_OK;
+  if (n == 0) {
+    if (!done_event) return T5E_OK;
+    const cudaError_t e0 = cudaEventRecord(done_event, static_cast<cudaStream_t>(stream));
+    if (e0 != cudaSuccess) {
+      set_cuda_error("t5e_mma_dot_batch_staged_async event", e0);
+      return T5E_ERR_CUDA;
+    }
+    return T5E_OK;
+  }
   if (!host->a || !host->b || !host->c || !host->d) return T5E_ERR_INVALID;
   if (host->nscale > 0 && (!host->scale_a || !host->scale_b)) return T5E_ERR_INVALID;
   if (host->sparse != 0 && !host->metadata) return T5E_ERR_INVALID;
@@ -334,15 +350,42 @@ int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, cons
     set_cuda_error("t5e_mma_dot_batch_staged copy", e);
     rc = T5E_ERR_CUDA;
   }
-  // every copy and kernel this call queued has finished when it returns
-  const cudaError_t e_up = cudaStreamSynchronize(cs.up);
-  const cudaError_t e_down = cudaStreamSynchronize(cs.down);
-  if (rc == T5E_OK && (e_up != cudaSuccess || e_down != cudaSuccess)) {
-    set_cuda_error("t5e_mma_dot_batch_staged synchronize", e_up != cudaSuccess ? e_up : e_down);
-    rc = T5E_ERR_CUDA;
+  if (rc == T5E_OK && done_event) {
+    // queued: the caller's event marks the last download
+    e = cudaEventRecord(done_event, cs.down);
+    if (e != cudaSuccess) {
+      set_cuda_error("t5e_mma_dot_batch_staged_async event", e);
+      rc = T5E_ERR_CUDA;
+    }
   }
+  if (!done_event || rc != T5E_OK) {
+    // synchronous, or failed: every copy and kernel this call queued has
+    // finished when it returns
+    const cudaError_t e_up = cudaStreamSynchronize(cs.up);
+    const cudaError_t e_down = cudaStreamSynchronize(cs.down);
+    if (rc == T5E_OK && (e_up != cudaSuccess || e_down != cudaSuccess)) {
+      set_cuda_error("t5e_mma_dot_batch_staged synchronize", e_up != cudaSuccess ? e_up : e_down);
+      rc = T5E_ERR_CUDA;
+    }
+  }
+  // events still pending are released by the runtime once they complete
   for (cudaEvent_t x : ev) cudaEventDestroy(x);
   return rc;
+}
+
+}  // namespace t5e
+
+extern "C" {
+
+int t5e_mma_dot_batch_staged(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
+                             uint64_t chunk_cases, void* stream) {
+  return staged_run(model, host, dev, chunk_cases, stream, nullptr);
+}
+
+int t5e_mma_dot_batch_staged_async(const t5e_model* model, const t5e_batch* host, const t5e_batch* dev,
+                                   uint64_t chunk_cases, void* stream, void* done_event) {
+  if (!done_event) return T5E_ERR_INVALID;
+  return staged_run(model, host, dev, chunk_cases, stream, static_cast<cudaEvent_t>(done_event));
 }
 
 int t5e_pack_rows(int32_t format, const uint32_t* words, uint64_t rows, int32_t k, void* out, int64_t out_stride,

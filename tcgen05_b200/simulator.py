@@ -344,6 +344,33 @@ def mma(
 # ----------------------------------------------------------- batched API
 
 
+class PendingBatch:
+    """Result words of a host batch that ``mma_dot_batch(..., wait=False)``
+    left in flight.  ``wait()`` blocks until every word is in ``out`` and
+    returns it; ``ready()`` polls.  The device buffers the batch streams
+    through stay referenced here until then, so that the allocator cannot
+    hand them out while a copy still reads them; dropping an unfinished
+    batch therefore waits for it."""
+
+    def __init__(self, out, event=None, buffers=None):
+        self.out = out
+        self._event = event
+        self._buffers = buffers
+
+    def ready(self) -> bool:
+        return self._buffers is None or self._event.query()
+
+    def wait(self):
+        if self._buffers is not None:
+            self._event.synchronize()
+            self._buffers = None
+        return self.out
+
+    def __del__(self):
+        if getattr(self, "_buffers", None) is not None:
+            self._event.synchronize()
+
+
 class PackedRows:
     """Operand rows already in the kernels' packed layout (see packing.py):
     ``data`` is a [rows, stride] uint8 array or tensor, ``k`` the elements per
@@ -437,6 +464,11 @@ def _pinned(x) -> bool:
 # chunks keep the host-to-device copies back to back.
 PIPELINE_MIN_CASES = 1 << 16
 PIPELINE_CHUNKS = 4
+# Batches left in flight (wait=False) overlap with the next batch's upload,
+# so each needs fewer chunks of its own: fewer, larger copies keep the link
+# closer to its plain-copy rate (measured: 53 GB/s with 1-2 chunks, 52 with
+# 4, 50 with 8, for 70 MB batches back to back).
+PIPELINE_CHUNKS_IN_FLIGHT = 2
 
 _COPY_STREAMS: dict = {}
 
@@ -453,14 +485,16 @@ def _copy_streams(dev):
 
 
 def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n, dev, out, check, meta_error,
-                     generic):
+                     generic, wait=True):
     """Host-resident batch in pinned memory -> pinned ``out``: the cases are
     cut into chunks; each chunk's operands are copied to the device on one
     stream, evaluated on the current stream once its copy has landed, and its
     result words (and status bytes) copied back on a third stream, so the
     copies in both directions overlap each other and the kernels.  The
     library's t5e_mma_dot_batch_staged runs that loop; the loop below it
-    serves the generic kernel and metadata shared by every case."""
+    serves the generic kernel and metadata shared by every case.  With
+    ``wait`` false and no per-case status to read back, the library call
+    returns once everything is queued and a PendingBatch is returned."""
     import torch
 
     comp = torch.cuda.current_stream(dev)
@@ -484,7 +518,7 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
     lib = nat.load()
     fn = lib.t5e_mma_dot_batch_generic if generic else lib.t5e_mma_dot_batch
     handle = ctypes.c_void_p(comp.cuda_stream)
-    step = -(-n // PIPELINE_CHUNKS)
+    step = -(-n // (PIPELINE_CHUNKS if wait or check else PIPELINE_CHUNKS_IN_FLIGHT))
     step = (step + 1023) // 1024 * 1024
     sa_h = None if sa is None else sa.view(torch.uint8)
     sb_h = None if sb is None else sb.view(torch.uint8)
@@ -503,6 +537,14 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
             hb.metadata = meta.view(torch.int32)
         dev_struct = runtime.make_batch_struct(db, d_dev, st_dev)
         host_struct = runtime.make_batch_struct(hb, out, st_host)
+        if not wait and not check:
+            done = torch.cuda.Event()
+            done.record(comp)  # creates the event; the library records it again after the last download
+            nat.check(lib.t5e_mma_dot_batch_staged_async(ctypes.byref(desc), ctypes.byref(host_struct),
+                                                         ctypes.byref(dev_struct), step, handle,
+                                                         ctypes.c_void_p(done.cuda_event)),
+                      "t5e_mma_dot_batch_staged_async")
+            return PendingBatch(out, done, (a_dev, b_dev, c_dev, sa_dev, sb_dev, meta_dev, d_dev))
         nat.check(lib.t5e_mma_dot_batch_staged(ctypes.byref(desc), ctypes.byref(host_struct), ctypes.byref(dev_struct),
                                                step, handle), "t5e_mma_dot_batch_staged")
         if check:
@@ -573,6 +615,7 @@ def mma_dot_batch(
     check: bool = True,
     generic: bool = False,
     out=None,
+    wait: bool = True,
 ):
     """N independent ``mma_dot`` evaluations in one kernel launch.
 
@@ -586,7 +629,26 @@ def mma_dot_batch(
     torch.uint32 CUDA tensor for device inputs, or ``out`` (a host array or
     pinned tensor of N 32-bit words) filled in place.  With ``check`` the
     per-case ValueErrors of the reference are raised.
+
+    ``wait=False`` returns a ``PendingBatch`` instead; its ``wait()`` returns
+    what the call would have.  A batch streamed from pinned host memory
+    (``PackedRows`` over pinned tensors and a pinned ``out``) then returns
+    as soon as its copies and kernels are queued, so that the next batch's
+    upload follows on the link without a gap.  Sparse batches with
+    ``check`` need their status bytes on the host and complete before
+    returning, as do all other inputs.
     """
+    res = _mma_dot_batch(a, b, c, model=model, a_format=a_format, b_format=b_format, d_type=d_type,
+                         saturate=saturate, scaling=scaling, scale_vec=scale_vec, kind=kind, scale_a=scale_a,
+                         scale_b=scale_b, sparse_metadata=sparse_metadata, device=device, check=check,
+                         generic=generic, out=out, wait=wait)
+    if not wait and not isinstance(res, PendingBatch):
+        res = PendingBatch(res)
+    return res
+
+
+def _mma_dot_batch(a, b, c, *, model, a_format, b_format, d_type, saturate, scaling, scale_vec, kind, scale_a,
+                   scale_b, sparse_metadata, device, check, generic, out, wait):
     import torch
 
     selected = model or make_model(a_format, b_format, d_type=d_type, saturate=saturate, scaling=scaling,
@@ -633,7 +695,7 @@ def mma_dot_batch(
         sa_p = scale_a if desc.family in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED) else None
         sb_p = scale_b if sa_p is not None else None
         return _pipelined_batch(selected, desc, a, b, c.reshape(n), sa_p, sb_p, meta, flags, sparse, k, n, dev, out,
-                                check, meta_error_p, generic)
+                                check, meta_error_p, generic, wait)
     if streamed:
         a_rows, _, _ = _operand_rows(a, desc.a_format, dev, "A")
         b_rows, _, _ = _operand_rows(b, desc.b_format, dev, "B")

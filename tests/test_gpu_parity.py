@@ -477,6 +477,65 @@ def test_full_size_fast_equals_generic_and_shards(name):
     assert_words_equal(fast[sample], oracle.eval_cases(cases.subset(sample)), name + " sample vs oracle")
 
 
+def _pinned_batch(name, n, seed):
+    """A configuration's cases as pinned host PackedRows, C and keyword
+    arguments for mma_dot_batch: (cases, pa, pb, c, kw)."""
+    import torch
+
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import packing
+
+    cases = workloads.config_cases(name, n, seed=seed)
+    d = full_desc(cases.desc)
+    model = t5.make_model(d["a_format"], d["b_format"], d_type=d["d_type"], saturate=d["saturate"],
+                          scaling=d["scaling"], scale_vec=d["scale_vec"], kind=d["kind"])
+    desc = model.descriptor()
+    a = cases.a
+    compressed = False
+    if cases.meta is not None:
+        act = workloads.active_mask(cases.meta, cases.k, "4of8")
+        a = cases.a[act].reshape(n, -1)
+        compressed = True
+    pa = t5.PackedRows(torch.from_numpy(packing.pack_rows(a, desc.a_format)).pin_memory(), a.shape[1], compressed)
+    pb = t5.PackedRows(torch.from_numpy(packing.pack_rows(cases.b, desc.b_format)).pin_memory(), cases.k)
+    f16 = desc.d_type == nat.D_F16
+    c = torch.from_numpy((cases.c & 0xFFFF).astype(np.uint16).view(np.int16) if f16 else cases.c.view(np.int32))
+    kw = {kk: d[kk] for kk in KEYS}
+    if cases.scale_a is not None:
+        kw["scale_a"] = torch.from_numpy(cases.scale_a).pin_memory()
+        kw["scale_b"] = torch.from_numpy(cases.scale_b).pin_memory()
+    if cases.meta is not None:
+        kw["sparse_metadata"] = torch.from_numpy(cases.meta.view(np.int32)).pin_memory()
+    return cases, pa, pb, c.pin_memory(), kw
+
+
+@pytest.mark.parametrize("name", ["e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "nvfp4-sparse-k128", "u8xs8-k32-wrap"])
+def test_pinned_host_batches_in_flight_together(name):
+    """wait=False: three streamed batches queued back to back, then waited
+    for; each one's words equal the one-piece evaluation.  Sparse batches run
+    with check=False so that they stay in flight; with check they complete
+    before the call returns.  Dropping an unfinished batch waits for it."""
+    import torch
+
+    batches = [_pinned_batch(name, (1 << 18) + 333 * i, seed=40 + i) for i in range(3)]
+    outs = [torch.full((b[0].n,), -1, dtype=torch.int32).pin_memory() for b in batches]
+    pending = [t5.mma_dot_batch(pa, pb, c, out=o, wait=False, check=False, **kw)
+               for (cases, pa, pb, c, kw), o in zip(batches, outs)]
+    assert all(isinstance(p, t5.PendingBatch) for p in pending)
+    for p, o, (cases, *_rest) in zip(pending, outs, batches):
+        assert p.wait() is o and p.ready()
+        assert_words_equal(o.numpy().view(np.uint32), gpu_cases(cases), name + " in flight vs one piece")
+    cases, pa, pb, c, kw = batches[0]
+    o = torch.full((cases.n,), -1, dtype=torch.int32).pin_memory()
+    p = t5.mma_dot_batch(pa, pb, c, out=o, wait=False, check=False, **kw)
+    del p
+    assert_words_equal(o.numpy().view(np.uint32), outs[0].numpy().view(np.uint32), name + " dropped batch")
+    p = t5.mma_dot_batch(pa, pb, c, out=o, wait=False, **kw)  # check=True
+    if cases.meta is not None:
+        assert p.ready()  # a checked sparse batch reads its status bytes back before returning
+    assert p.wait() is o
+
+
 @pytest.mark.parametrize("name", ["e4m3xe5m2-k32-f16", "nvfp4-sparse-k128", "u8xs8-k32-wrap"])
 def test_pinned_host_batches_stream_in_chunks(name):
     """Pinned host operands, C and output take the chunked copy/compute

@@ -131,3 +131,8 @@ def test_issue_probe_counts_its_instructions():
         assert lib.t5e_issue_probe(pipe, 4, ctypes.byref(count), None) == nat.OK
         torch.cuda.synchronize()
         assert count.value == sms * 2 * 32 * 4 * 256
+
+
+def test_staged_async_needs_an_event_without_a_device():
+    lib = nat.load()
+    assert lib.t5e_mma_dot_batch_staged_async(None, None, None, 0, None, None) == nat.ERR_INVALID
