@@ -325,9 +325,9 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) raw_window_kernel(cons
       // the rows of this lane's case in the warp's next tile start moving
       // into L2 while this tile is classified and accumulated
       prefetch_case<AF, BF, F16D>(B, i + warps * 32u, n);
-      // byte-SIMD flags, bit 7 of each byte: NaN codes, infinite codes, an
-      // infinity times a zero, infinite products of each sign
-      uint32_t nan = 0, inf = 0, inf_zero = 0, inf_pos = 0, inf_neg = 0;
+      // byte-SIMD flags, bit 7 of each byte: NaN codes, an infinity times a
+      // zero, infinite products of each sign (an infinite code is one of them)
+      uint32_t nan = 0, inf_zero = 0, inf_pos = 0, inf_neg = 0;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
         if constexpr (SA::kAny) nan |= SA::nan7(ca[w]);
@@ -337,7 +337,6 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) raw_window_kernel(cons
           const uint32_t ib = SB::kInf ? SB::inf7(cb[w]) : 0u;
           const uint32_t any = ia | ib;
           const uint32_t sgn = Code<AF>::sign(ca[w]) ^ Code<BF>::sign(cb[w]);
-          inf |= any;
           inf_zero |= (ia & Code<BF>::zero(cb[w])) | (ib & Code<AF>::zero(ca[w]));
           inf_neg |= any & sgn;
           inf_pos |= any & ~sgn;
@@ -347,7 +346,7 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) raw_window_kernel(cons
       const bool c_neg = (cw & c_sign) != 0;
       bool is_nan = (nan & 0x80808080u) || scale_nan || (c_special && (cw & c_frac));
       uint32_t special = 0xFFFFFFFFu;
-      if ((inf & 0x80808080u) != 0) {
+      if (((inf_pos | inf_neg) & 0x80808080u) != 0) {
         // an infinite product makes the result special whatever the finite
         // terms are: NaN for Inf x 0 or infinities of both signs (C
         // included), else the signed infinity (model.py:416-436)
