@@ -233,6 +233,21 @@ __device__ __forceinline__ uint32_t round_f16_rne(int64_t units, int q) {
   return sign | (uint32_t)rm;
 }
 
+// units * 2**q -> F16 word, round to nearest even, for |units| < 2**53 and a
+// scaled value inside the double range: the double units * 2**q is exact, so
+// one hardware conversion rounds it once, as round_f16_rne does (overflow to
+// infinity, subnormals in steps of 2**-24).  The reference returns an
+// unsigned zero when the magnitude rounds to zero (model.py:347-348); the
+// conversion keeps the sign there, so that word is cleared.
+__device__ __forceinline__ uint32_t round_f16_rne_exact(int64_t units, int q) {
+  if (units == 0) return 0u;
+  const uint64_t bits = (uint64_t)__double_as_longlong((double)units) + ((uint64_t)(int64_t)q << 52);
+  unsigned short h;
+  asm("cvt.rn.f16.f64 %0, %1;" : "=h"(h) : "d"(__longlong_as_double((long long)bits)));
+  const uint32_t w = h;
+  return (w & 0x7FFFu) ? w : 0u;
+}
+
 // Exact sum of terms m * 2**e kept as (units, base exponent).
 struct ExactSum {
   int64_t units;

@@ -583,3 +583,31 @@ def test_pinned_host_batches_stream_in_chunks(name):
         kw["sparse_metadata"] = torch.from_numpy(bad.view(np.int32)).pin_memory()
         with pytest.raises(ValueError):
             t5.mma_dot_batch(pa, pb, c.pin_memory(), out=out, **kw)
+
+
+@pytest.mark.parametrize("a_format,b_format", [("e4m3", "e5m2"), ("e2m1", "e4m3"), ("e5m2", "e5m2")])
+def test_f16_d_rounding_edges(a_format, b_format):
+    """F16 D from the raw-window kernel at the rounding edges: subnormal
+    products and their ties, negative values that round to zero (the
+    reference returns an unsigned zero there), overflow around 65504/65520
+    and C words at the ends of the F16 range; against the oracle and the
+    generic kernel."""
+    rng = np.random.Generator(np.random.PCG64(1616))
+    n, k = 60000, 32
+    small = {"e4m3": [0x00, 0x01, 0x02, 0x03, 0x07, 0x08, 0x81, 0x82, 0x83, 0x87, 0x88, 0x7E, 0xFE, 0x40, 0xC0],
+             "e5m2": [0x00, 0x01, 0x02, 0x03, 0x04, 0x81, 0x82, 0x83, 0x84, 0x7B, 0xFB, 0x3C, 0xBC],
+             "e2m1": [0x0, 0x1, 0x2, 0x7, 0x8, 0x9, 0xA, 0xF]}
+    # most elements zero, so that one or two tiny or huge products decide the sum
+    def operand(fmt):
+        codes = np.array(small[fmt], dtype=np.uint32)
+        a = codes[rng.integers(0, len(codes), size=(n, k))]
+        a[rng.random((n, k)) < 0.9] = 0
+        return a
+    a, b = operand(a_format), operand(b_format)
+    c_words = np.array([0x0000, 0x8000, 0x0001, 0x8001, 0x0002, 0x8002, 0x03FF, 0x83FF, 0x0400, 0x8400,
+                        0x7BFF, 0xFBFF, 0x7BFE, 0x3C00, 0xBC00], dtype=np.uint32)
+    c = c_words[rng.integers(0, len(c_words), size=n)]
+    cases = workloads.Cases(dict(a_format=a_format, b_format=b_format, d_type="f16"), a, b, c)
+    got = gpu_cases(cases)
+    assert_words_equal(got, oracle.eval_cases(cases), f"{a_format}x{b_format} F16 D edges vs oracle")
+    assert_words_equal(got, gpu_cases(cases, generic=True), f"{a_format}x{b_format} F16 D edges vs generic")
