@@ -368,7 +368,10 @@ class PendingBatch:
 
     def __del__(self):
         if getattr(self, "_buffers", None) is not None:
-            self._event.synchronize()
+            try:
+                self._event.synchronize()
+            except Exception:  # interpreter shutdown: the CUDA context may already be gone
+                pass
 
 
 class PackedRows:
