@@ -104,7 +104,7 @@ __device__ __forceinline__ int64_t shift_trunc(int32_t m, int d) {
 // Whether some nonzero product among the 16 elements of (wa[0..1], wb[0..1])
 // has a_raw + b_raw > t, for 0 <= t <= 3.  Byte sums of the kRaw tables are
 // 8 + a_raw + b_raw when both elements are nonzero and at most 6 otherwise.
-__device__ __noinline__ bool block_exceeds(uint32_t wa0, uint32_t wa1, uint32_t wb0, uint32_t wb1, int t) {
+__device__ __forceinline__ bool block_exceeds(uint32_t wa0, uint32_t wa1, uint32_t wb0, uint32_t wb1, int t) {
   const uint32_t bias = (uint32_t)(128 - (t + 9)) * 0x01010101u;
   const uint32_t a0 = wa0 & 0x77777777u, a1 = wa1 & 0x77777777u;
   const uint32_t b0 = wb0 & 0x77777777u, b1 = wb1 & 0x77777777u;
