@@ -281,10 +281,19 @@ template <int AF, int BF, bool F16D, bool SCALED>
 __global__ void __launch_bounds__(kThreads, kBlocksPerSm) raw_window_kernel(const t5e_batch B) {
   extern __shared__ __align__(16) uint8_t smem[];
   constexpr int kShift = 25 - FracBits<AF>::value - FracBits<BF>::value;
-  // the first tile's rows move toward L2 while the tables are built
+  // A launch that follows on the same stream may start its blocks (and build
+  // its tables) on the SMs this grid leaves while its last tiles finish.
+  asm volatile("griddepcontrol.launch_dependents;");
+  // the first tile's rows move toward L2 while the tables are built (a
+  // prefetch into L2, the coherence point, reads nothing into the SM)
   prefetch_case<AF, BF, F16D>(B, (blockIdx.x * kWarps + (threadIdx.x >> 5)) * 32u + (threadIdx.x & 31u),
                               (uint32_t)B.n);
   build_lut<AF, BF>(smem, reinterpret_cast<uint2*>(smem + kLutBytes), kShift);  // staging in the queue area
+  // When launched as a programmatic dependent of the previous grid on the
+  // stream, wait here for that grid to complete and its writes to be
+  // visible before any operand is read or any result written; otherwise
+  // this returns at once.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
 
   using R = Rows<AF, BF>;
@@ -403,7 +412,23 @@ int launch_raw(const t5e_batch& B, cudaStream_t stream) {
   const uint64_t want = (tiles + kWarps - 1) / kWarps;
   const uint64_t cap = (uint64_t)kBlocksPerSm * (uint64_t)sms;  // resident blocks
   const int grid = (int)(want < cap ? (want ? want : 1) : cap);
-  kern<<<grid, kThreads, smem, stream>>>(B);
+  // programmatic stream serialisation: the kernel waits for the previous
+  // grid itself (griddepcontrol.wait) before touching global memory
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, B);
+  if (e != cudaSuccess) {
+    set_cuda_error("raw_window_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("raw_window_kernel launch");
 }
 
