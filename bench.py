@@ -42,6 +42,7 @@ WORKLOAD = "e4m3xe5m2-k32"
 VARIANTS = ("e4m3xe5m2-k32", "e4m3xe5m2-k32-f16")
 K_ELEMS = 32
 INPUT_SETS = 4
+E2E_RUNS = 3
 
 
 def algorithmic_bytes(variant: str, n: int) -> int:
@@ -294,13 +295,16 @@ def run_ours(args) -> int:
             p.wait()
 
     e2e_run(e2e_steps)  # the same calls once untimed: the allocator then holds every buffer the timed run needs
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(device)
-    t0 = time.perf_counter()
-    e2e_run(e2e_steps)
-    torch.cuda.synchronize(device)
-    e2e_s = time.perf_counter() - t0
+    e2e_runs = []
+    for _ in range(E2E_RUNS):  # the host link's rate varies from run to run: the median of three is reported
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        e2e_run(e2e_steps)
+        torch.cuda.synchronize(device)
+        e2e_runs.append(time.perf_counter() - t0)
+    e2e_s = statistics.median(e2e_runs)
     ok_e2e = all(np.array_equal(out.numpy(), item["d"].cpu().numpy()) for item, _, _, _, out in host)
 
     if world > 1:
@@ -373,6 +377,7 @@ def run_ours(args) -> int:
                          "binds": max(fracs, key=fracs.get)},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "steps": e2e_steps,
+                    "runs_s": e2e_runs, "reported": "median of the runs",
                     "calls": "mma_dot_batch(pinned PackedRows, pinned out, wait=False) per batch, every wait "
                              "inside the timed region"},
             "clocks": clocks,
