@@ -135,6 +135,11 @@ __device__ __forceinline__ uint32_t eval_rows(const uint32_t (&wa)[8], const uin
 
 template <int F, bool F16D, bool TILED>
 __global__ void __launch_bounds__(kThreads) wide_kernel(const t5e_batch B, int floor_raw) {
+  // Launched as a programmatic dependent of the previous kernel on the
+  // stream: let the next launch start its blocks early, and wait for the
+  // previous grid to complete before any operand is read.
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t n = (uint32_t)B.n;
   const uint32_t stride = gridDim.x * blockDim.x;
   const uint32_t per = (uint32_t)B.tile_m * (uint32_t)B.tile_n;
@@ -323,7 +328,20 @@ int launch(const t5e_batch& B, int floor_raw, cudaStream_t stream) {
   const uint64_t need = (B.n + kThreads - 1) / kThreads;
   const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
   const int grid = (int)(need < cap ? (need ? need : 1) : cap);
-  wide_kernel<F, F16D, TILED><<<grid, kThreads, 0, stream>>>(B, floor_raw);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, wide_kernel<F, F16D, TILED>, B, floor_raw);
+  if (e != cudaSuccess) {
+    set_cuda_error("wide_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("wide_kernel launch");
 }
 
