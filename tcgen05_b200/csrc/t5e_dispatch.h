@@ -36,6 +36,27 @@ int grid_for(uint64_t n, int block);
 // would return), made without any CUDA call.
 int validate(const t5e_model* M, const t5e_batch* B);
 
+// Launches `kernel` on `stream` as a programmatic dependent of the previous
+// kernel there (programmatic stream serialisation): its blocks may start
+// while that kernel's last blocks run, so the kernel must execute
+// griddepcontrol.wait before it reads or writes global memory that earlier
+// work on the stream may touch.
+template <typename... Params, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(Params...), unsigned grid, unsigned block, size_t smem,
+                             cudaStream_t stream, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // Raises Kernel's dynamic shared-memory limit to `bytes` on the current
 // device, once per device and kernel (one flag array per kernel; host
 // threads may race to set it, which is harmless: the attribute value is the

@@ -537,7 +537,11 @@ __device__ __forceinline__ void mx_entries(const uint8_t* smem, uint32_t ca, uin
 template <int AF, int BF>
 __global__ void __launch_bounds__(kMxThreads, 1) mx_kernel(const t5e_batch B) {
   extern __shared__ __align__(16) uint8_t smem[];
+  // programmatic dependent launch: signal the next launch, build the table,
+  // then wait for the previous grid before touching global memory
+  asm volatile("griddepcontrol.launch_dependents;");
   build_mx_lut<AF, BF>(reinterpret_cast<uint32_t*>(smem));
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   __syncthreads();
   using R = Rows<AF, BF>;
   constexpr int kU = MxUnit<AF>::value + MxUnit<BF>::value;
@@ -644,7 +648,11 @@ int launch_mx(const t5e_batch& B, cudaStream_t stream) {
   const uint64_t want = (tiles + kMxWarps - 1) / kMxWarps;
   const uint64_t cap = (uint64_t)sms;  // one resident block per SM
   const int grid = (int)(want < cap ? (want ? want : 1) : cap);
-  kern<<<grid, kMxThreads, smem, stream>>>(B);
+  const cudaError_t e = launch_dependent(kern, (unsigned)grid, kMxThreads, (size_t)smem, stream, B);
+  if (e != cudaSuccess) {
+    set_cuda_error("mx_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("mx_kernel launch");
 }
 

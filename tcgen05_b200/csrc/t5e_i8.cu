@@ -34,6 +34,9 @@ __device__ __forceinline__ int32_t dot4(uint32_t a, uint32_t b, int32_t c) {
 
 template <bool AS, bool BS, bool SAT>
 __global__ void __launch_bounds__(kThreads) i8_kernel(const t5e_batch B) {
+  // programmatic dependent launch: no prologue, so wait for the previous grid at once
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t n = (uint32_t)B.n;
   const uint32_t stride = gridDim.x * blockDim.x;
   const int chunks = B.k / 16;
@@ -68,7 +71,11 @@ int launch(const t5e_batch& B, cudaStream_t stream) {
   const uint64_t need = (B.n + kThreads - 1) / kThreads;
   const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
   const int grid = (int)(need < cap ? (need ? need : 1) : cap);
-  i8_kernel<AS, BS, SAT><<<grid, kThreads, 0, stream>>>(B);
+  const cudaError_t e = launch_dependent(i8_kernel<AS, BS, SAT>, (unsigned)grid, kThreads, 0, stream, B);
+  if (e != cudaSuccess) {
+    set_cuda_error("i8_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("i8_kernel launch");
 }
 
