@@ -235,3 +235,41 @@ def test_device_config_generators_follow_the_configurations():
             assert db.sparse == nat.SPARSE_4OF8 and db.flags & nat.FLAG_SPARSE_A_COMPRESSED
         macs, nbytes = workloads.config_work(name, db)
         assert macs == n * (64 if name.startswith("nvfp4") else db.k)
+
+
+class _FakeEvent:
+    """Stands in for a CUDA event: records the calls a PendingBatch makes."""
+
+    def __init__(self, done=False, fail=False):
+        self.done, self.fail, self.waits = done, fail, 0
+
+    def query(self):
+        return self.done
+
+    def synchronize(self):
+        self.waits += 1
+        if self.fail:
+            raise RuntimeError("context gone")
+        self.done = True
+
+
+def test_pending_batch_completed_and_in_flight():
+    out = np.zeros(4, dtype=np.uint32)
+    done = t5.PendingBatch(out)  # what wait=False returns for a batch that completed in the call
+    assert done.ready() and done.wait() is out
+    ev = _FakeEvent()
+    p = t5.PendingBatch(out, ev, ("buffers",))
+    assert not p.ready()
+    assert p.wait() is out and ev.waits == 1
+    assert p.ready() and p.wait() is out and ev.waits == 1  # the buffers were released once
+
+
+def test_dropping_a_pending_batch_waits_and_tolerates_teardown():
+    ev = _FakeEvent()
+    p = t5.PendingBatch(np.zeros(1), ev, ("buffers",))
+    del p
+    assert ev.waits == 1
+    gone = _FakeEvent(fail=True)
+    p = t5.PendingBatch(np.zeros(1), gone, ("buffers",))
+    del p  # an event that can no longer be waited on (interpreter exit) raises nothing
+    assert gone.waits == 1
