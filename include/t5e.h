@@ -219,7 +219,8 @@ int t5e_mma_dot_batch_staged_async(const t5e_model* model, const t5e_batch* host
  * T5E_NOALLOC_STAGE_BYTES that every GPU loading the library holds until the
  * process exits; the result region is cleared, the batch evaluated as by
  * t5e_mma_dot_batch, and the D words (and status bytes) copied back.  Returns
- * when they are in host memory.  A batch whose regions (each rounded up to
+ * when they are in host memory: the call synchronizes `stream` before it
+ * returns, on success and on every error after its first copy was queued.  A batch whose regions (each rounded up to
  * 256 bytes) do not fit in the array is rejected with T5E_ERR_INVALID and a
  * message in t5e_last_error().  Calls no allocator.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, with

@@ -125,6 +125,9 @@ extern "C" int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch
   if (e == cudaSuccess && st_bytes) e = cudaMemsetAsync(base + off_st, 0, st_bytes, s);
   if (e != cudaSuccess) {
     set_cuda_error("t5e_mma_dot_batch_noalloc: staging copy", e);
+    // copies queued before the failing one may still read the caller's
+    // buffers and write the shared array, which the next call reuses
+    cudaStreamSynchronize(s);
     return T5E_ERR_CUDA;
   }
   t5e_batch dev_batch = *host;
@@ -143,7 +146,9 @@ extern "C" int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch
   }
   e = cudaMemcpyAsync(host->d, base + off_d, d_bytes, cudaMemcpyDeviceToHost, s);
   if (e == cudaSuccess && st_bytes) e = cudaMemcpyAsync(host->status, base + off_st, st_bytes, cudaMemcpyDeviceToHost, s);
-  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  // every path returns with this call's copies and kernel finished
+  const cudaError_t e_sync = cudaStreamSynchronize(s);
+  if (e == cudaSuccess) e = e_sync;
   if (e != cudaSuccess) {
     set_cuda_error("t5e_mma_dot_batch_noalloc: result copy", e);
     return T5E_ERR_CUDA;

@@ -29,6 +29,8 @@
 //    permute selectors spread from the metadata nibbles.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "t5e_arith.cuh"
 #include "t5e_dispatch.h"
 
@@ -339,14 +341,17 @@ int launch(const t5e_batch& B, cudaStream_t stream) {
   int dev = 0, sms = 148, per_sm = 0;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  static int resident[64] = {};  // resident blocks per SM, queried once per device
-  if (dev >= 0 && dev < 64 && resident[dev]) {
-    per_sm = resident[dev];
+  // resident blocks per SM, queried once per device; host threads may race
+  // to fill an entry, which is harmless (they store the same value)
+  static std::atomic<int> resident[64];
+  const int cached = dev >= 0 && dev < 64 ? resident[dev].load(std::memory_order_relaxed) : 0;
+  if (cached) {
+    per_sm = cached;
   } else {
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, nvfp4_kernel<SPARSE, A_LOGICAL>, kThreads, 0) !=
             cudaSuccess || per_sm < 1)
       per_sm = 1;
-    if (dev >= 0 && dev < 64) resident[dev] = per_sm;
+    if (dev >= 0 && dev < 64) resident[dev].store(per_sm, std::memory_order_relaxed);
   }
   // one wave of resident blocks, each striding over the cases
   const uint64_t need = (B.n + kThreads - 1) / kThreads;

@@ -38,6 +38,27 @@ K_OF_KIND = {0: 8, 1: 16, 2: 32, 3: 32}
 C_FORMATS = {"f16": 0, "f32": 1, "s32": 2}
 SUB_BYTE = ("e2m3", "e3m2", "e2m1")
 
+# Set once a launch reports an expired wait.  The kernel then frees its tensor
+# memory while the tcgen05.mma it committed may still be writing there, so a
+# later launch in this process could read columns that product overwrites:
+# every result after a timeout is untrusted, and no further hardware tiles
+# are launched in the process.
+_WAIT_EXPIRED = False
+
+
+def _refuse_after_timeout() -> None:
+    if _WAIT_EXPIRED:
+        raise RuntimeError("an earlier tcgen05.mma product in this process did not complete within the kernel's "
+                           "bounded wait; no further hardware tiles are launched in this process")
+
+
+def _check_wait(err) -> None:
+    global _WAIT_EXPIRED
+    if int(err.item()):
+        _WAIT_EXPIRED = True
+        raise RuntimeError("a tcgen05.mma product did not complete within the kernel's bounded wait; results of "
+                           "this process's hardware tiles are untrusted from here on")
+
 
 def default_d_type(a_format: str) -> str:
     return "s32" if KINDS[a_format] == 3 else "f32"
@@ -91,6 +112,7 @@ def hardware_tiles(a, b, c, a_format: str, b_format: str | None = None, *, satur
     (row-major B), c [T, 128, 16] container words (uint32 numpy arrays; F16
     accumulators in the low 16 bits, and the hardware leaves the upper 16
     bits of an F16 accumulator column zero)."""
+    _refuse_after_timeout()
     import torch
 
     b_format = b_format or a_format
@@ -119,8 +141,7 @@ def hardware_tiles(a, b, c, a_format: str, b_format: str | None = None, *, satur
                                t, err.data_ptr(), stream)
     nat.check(rc, "t5e_tcgen05_tiles")
     torch.cuda.synchronize(dev)
-    if int(err.item()):
-        raise RuntimeError("a tcgen05.mma product did not complete within the kernel's bounded wait")
+    _check_wait(err)
     return d_dev.cpu().numpy().view(np.uint32).reshape(t, M, N)
 
 
@@ -275,6 +296,7 @@ def hardware_block_scaled_tiles(a, b, c, scale_a, scale_b, kind: str, a_format: 
     """D words of T block-scaled tiles computed by tcgen05.mma: a [T, 128, K],
     b [T, K, 128] (row-major B), c [T, 128, 128] F32 words, scale_a
     [T, 128, blocks] (per A row), scale_b [T, 128, blocks] (per B column)."""
+    _refuse_after_timeout()
     import torch
 
     b_format = b_format or a_format
@@ -302,8 +324,7 @@ def hardware_block_scaled_tiles(a, b, c, scale_a, scale_b, kind: str, a_format: 
                                             err.data_ptr(), stream)
     nat.check(rc, "t5e_tcgen05_block_scaled_tiles")
     torch.cuda.synchronize(dev)
-    if int(err.item()):
-        raise RuntimeError("a tcgen05.mma product did not complete within the kernel's bounded wait")
+    _check_wait(err)
     return d_dev.cpu().numpy().view(np.uint32).reshape(t, M, BS_N)
 
 

@@ -348,9 +348,10 @@ class PendingBatch:
     """Result words of a host batch that ``mma_dot_batch(..., wait=False)``
     left in flight.  ``wait()`` blocks until every word is in ``out`` and
     returns it; ``ready()`` polls.  The device buffers the batch streams
-    through stay referenced here until then, so that the allocator cannot
-    hand them out while a copy still reads them; dropping an unfinished
-    batch therefore waits for it."""
+    through, and the caller's pinned host inputs the uploads read, stay
+    referenced here until then, so that neither allocator can hand them out
+    while a copy still uses them (a caller may drop its inputs right after
+    the call); dropping an unfinished batch therefore waits for it."""
 
     def __init__(self, out, event=None, buffers=None):
         self.out = out
@@ -547,7 +548,11 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
                                                          ctypes.byref(dev_struct), step, handle,
                                                          ctypes.c_void_p(done.cuda_event)),
                       "t5e_mma_dot_batch_staged_async")
-            return PendingBatch(out, done, (a_dev, b_dev, c_dev, sa_dev, sb_dev, meta_dev, d_dev))
+            # the library's uploads read the caller's pinned inputs on its own stream, so the pinned-memory
+            # allocator records no use of them: they stay referenced here, with the device buffers, until the
+            # batch's event has fired, so that none can be freed and handed to a new allocation meanwhile
+            return PendingBatch(out, done, (a_dev, b_dev, c_dev, sa_dev, sb_dev, meta_dev, d_dev,
+                                            a.data, b.data, c, sa_h, sb_h, meta))
         nat.check(lib.t5e_mma_dot_batch_staged(ctypes.byref(desc), ctypes.byref(host_struct), ctypes.byref(dev_struct),
                                                step, handle), "t5e_mma_dot_batch_staged")
         if check:

@@ -266,6 +266,106 @@ def generate(spec: W.PathSpec, start: int, count: int, total: int, xp=np, device
     return out
 
 
+_SPARSE_MODE = {"1of2": 1, "2of4": 2, "4of8": 3}  # T5E_SPARSE_* of the selection modes
+
+
+def sparse_mode(spec: W.PathSpec) -> str | None:
+    """Selection mode of a sparse path ("1of2", "2of4", "4of8"), None if dense."""
+    fam = spec.family
+    if fam == "sparse":
+        return "1of2" if spec.params[0] == "tf32" else "2of4"
+    if fam == "sparse-mx":
+        return "2of4"
+    if fam in ("sparse-nvfp4", "sparse-fp4block"):
+        return "4of8"
+    return None
+
+
+def path_model(spec: W.PathSpec):
+    """The arithmetic model of a path (make_model with its descriptor)."""
+    from .model import make_model
+
+    d = spec.descriptor
+    return make_model(d["a_format"], d["b_format"], d_type=d["d_type"], saturate=d["saturate"],
+                      scaling=d["scaling"], scale_vec=d["scale_vec"], kind=d["kind"])
+
+
+def scale_blocks(spec: W.PathSpec, model=None) -> int:
+    """Scale bytes per operand row a case reaches: physical K over the
+    model's scale block (0 for unscaled paths)."""
+    from . import _native as nat
+
+    desc = (model or path_model(spec)).descriptor()
+    if desc.family not in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED):
+        return 0
+    return -(-_phys_k(spec) // desc.scale_block)
+
+
+def device_batch(spec: W.PathSpec, start: int, count: int, total: int, device):
+    """Cases [start, start + count) of a path with `total` cases, generated on
+    `device` (``generate``) and laid out as the kernels read them:
+    (model, DeviceBatch).  Sparse A rows hold only the selected elements
+    (physical K, T5E_SPARSE_A_COMPRESSED), B rows the logical K; scale rows
+    keep the blocks physical K reaches, metadata the words its chunks need.
+    The result words equal those of the public API on ``host_cases`` of the
+    same range."""
+    import torch
+
+    from . import _native as nat
+    from . import packing
+    from .runtime import DeviceBatch
+
+    model = path_model(spec)
+    desc = model.descriptor()
+    g = generate(spec, start, count, total, torch, device)
+    k = path_k(spec)
+    to32 = lambda x: torch.where(x >= 1 << 31, x - (1 << 32), x).to(torch.int32)  # noqa: E731
+    a = g["a"]
+    mode = sparse_mode(spec)
+    sparse = flags = 0
+    meta = None
+    if mode is not None:
+        act = _active(torch, g["meta"], k, mode)
+        a = a[act].reshape(count, k // 2)  # every legal record selects exactly half of the logical K
+        sparse = _SPARSE_MODE[mode]
+        flags = nat.FLAG_SPARSE_A_COMPRESSED
+        chunks = k // {"1of2": 2, "2of4": 4, "4of8": 8}[mode]
+        meta = to32(g["meta"][:, : -(-chunks // 8)]).contiguous()
+    f16 = desc.d_type == nat.D_F16
+    c = g["c"] & 0xFFFF if f16 else g["c"]
+    c = torch.where(c >= 1 << 15, c - (1 << 16), c).to(torch.int16) if f16 else to32(c)
+    db = DeviceBatch(n=count, k=k, a=packing.pack_rows_device(to32(a), desc.a_format),
+                     b=packing.pack_rows_device(to32(g["b"]), desc.b_format), c=c.contiguous(),
+                     metadata=meta, flags=flags, sparse=sparse)
+    blocks = scale_blocks(spec, model)
+    if blocks:
+        db.scale_a = g["scale_a"][:, :blocks].to(torch.uint8).contiguous()
+        db.scale_b = g["scale_b"][:, :blocks].to(torch.uint8).contiguous()
+    return model, db
+
+
+def path_work(spec: W.PathSpec, cases: int, model=None) -> tuple[int, int]:
+    """(element-MACs, algorithmic bytes) of `cases` cases of a path.  MACs are
+    the physical products; bytes follow the per-path formula: packed A at
+    physical K, packed B at logical K, C and D (2 bytes each for F16 D, else
+    4), one byte per scale block each operand reaches, half a byte per
+    metadata chunk."""
+    from . import _native as nat
+
+    model = model or path_model(spec)
+    desc = model.descriptor()
+    k = path_k(spec)
+    kp = _phys_k(spec)
+    bits = nat.FORMAT_BITS
+    cd = 2 if desc.d_type == nat.D_F16 else 4
+    per = -(-kp * bits[desc.a_format] // 8) + -(-k * bits[desc.b_format] // 8) + 2 * cd
+    per += 2 * scale_blocks(spec, model)
+    mode = sparse_mode(spec)
+    if mode is not None:
+        per += k // {"1of2": 2, "2of4": 4, "4of8": 8}[mode] // 2
+    return cases * kp, cases * per
+
+
 def host_cases(spec: W.PathSpec, start: int, count: int, total: int) -> W.Cases:
     """The numpy mirror of `generate` as public-API cases (for the oracle)."""
     g = generate(spec, start, count, total, np)

@@ -536,6 +536,30 @@ def test_pinned_host_batches_in_flight_together(name):
     assert p.wait() is o
 
 
+@pytest.mark.parametrize("name", ["e4m3xe5m2-k32", "nvfp4-sparse-k128"])
+def test_in_flight_batch_survives_dropped_inputs(name):
+    """A caller may drop its pinned inputs right after a wait=False call: the
+    PendingBatch keeps them alive until its uploads are done, so new pinned
+    allocations filled meanwhile (which could otherwise reuse those blocks)
+    do not change the result words, which equal the oracle's."""
+    import torch
+
+    from oracle import oracle
+
+    n = (1 << 20) + 4096
+    cases, pa, pb, c, kw = _pinned_batch(name, n, seed=77)
+    want = oracle.eval_cases(cases)
+    o = torch.full((n,), -1, dtype=torch.int32).pin_memory()
+    p = t5.mma_dot_batch(pa, pb, c, out=o, wait=False, check=False, **kw)
+    sizes = [pa.data.numel(), pb.data.numel(), c.numel() * c.element_size()]
+    sizes += [kw[k].numel() * kw[k].element_size() for k in ("scale_a", "scale_b", "sparse_metadata") if k in kw]
+    del pa, pb, c, kw
+    fresh = [torch.empty(s, dtype=torch.uint8).pin_memory().fill_(0xA5) for s in sizes for _ in range(2)]
+    assert p.wait() is o
+    del fresh
+    assert_words_equal(o.numpy().view(np.uint32), want, name + " in flight with its inputs dropped")
+
+
 @pytest.mark.parametrize("name", ["e4m3xe5m2-k32-f16", "nvfp4-sparse-k128", "u8xs8-k32-wrap"])
 def test_pinned_host_batches_stream_in_chunks(name):
     """Pinned host operands, C and output take the chunked copy/compute

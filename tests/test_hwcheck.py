@@ -93,6 +93,30 @@ def test_descriptor_and_shape_validation():
     assert a.shape == (2, 128, 32) and b.shape == (2, 32, 16) and int(c.max()) <= 0xFFFF
 
 
+def test_expired_wait_refuses_later_launches(monkeypatch):
+    """After a launch reports an expired wait, the process launches no further
+    hardware tiles: both entry points raise before touching the device."""
+
+    class _Flag:
+        def __init__(self, v):
+            self.v = v
+
+        def item(self):
+            return self.v
+
+    monkeypatch.setattr(hwcheck, "_WAIT_EXPIRED", False)
+    hwcheck._check_wait(_Flag(0))
+    assert not hwcheck._WAIT_EXPIRED
+    with pytest.raises(RuntimeError, match="untrusted"):
+        hwcheck._check_wait(_Flag(1))
+    assert hwcheck._WAIT_EXPIRED
+    a, b, c = hwcheck.random_tiles("bf16", None, 1, 0)
+    with pytest.raises(RuntimeError, match="no further hardware tiles"):
+        hwcheck.hardware_tiles(a, b, c, "bf16")
+    with pytest.raises(RuntimeError, match="no further hardware tiles"):
+        hwcheck.hardware_block_scaled_tiles(None, None, None, None, None, "mxf4", "e2m1")
+
+
 def test_sub_byte_rows_have_the_f8f6f4_shared_memory_form():
     rng = np.random.default_rng(3)
     for fmt, bits in (("e2m1", 4), ("e2m3", 6), ("e3m2", 6)):
