@@ -17,6 +17,9 @@ int launch_fast(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 // The NVFP4 kernel (t5e_nvfp4.cu); same contract as launch_fast.
 int launch_nvfp4(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 
+// The UE8M0 MXF4-family kernel (t5e_mxf4.cu); same contract as launch_fast.
+int launch_mxf4(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
+
 // The kind::i8 kernel (t5e_i8.cu); same contract as launch_fast.
 int launch_i8(const t5e_model& M, const t5e_batch& B, cudaStream_t stream);
 

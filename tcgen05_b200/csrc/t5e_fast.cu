@@ -691,6 +691,11 @@ bool rows_fit(const t5e_batch& B, int af, int bf) {
 int launch_fast(const t5e_model& M, const t5e_batch& B, cudaStream_t stream) {
   using namespace fast;
   if (M.family == T5E_FAMILY_NVFP4) return launch_nvfp4(M, B, stream);
+  if (M.family == T5E_FAMILY_BLOCK_SCALED && M.a_format == T5E_FMT_E2M1 && M.b_format == T5E_FMT_E2M1 &&
+      M.product_merge_group != 0) {
+    const int rc = launch_mxf4(M, B, stream);
+    if (rc != T5E_ERR_UNSUPPORTED) return rc;
+  }
   if (M.family == T5E_FAMILY_I8) return launch_i8(M, B, stream);
   if (M.family == T5E_FAMILY_RAW_WINDOW && M.a_format <= T5E_FMT_F16) return launch_wide(M, B, stream);
   if (B.sparse != 0 || B.tile_m != 1 || B.tile_n != 1) return T5E_ERR_UNSUPPORTED;

@@ -434,18 +434,27 @@ def _nvfp4_adversarial(rng, n, sparse):
     return a, b, c, sa, sb, meta
 
 
+E2M1_KINDS = {"nvfp4": dict(a_format="e2m1", scaling="ue4m3", scale_vec=4),
+              "mxf4": dict(a_format="e2m1", scaling="ue8m0", kind="mxf4", scale_vec=2),
+              "mxf4nvf4-2x": dict(a_format="e2m1", scaling="ue8m0", kind="mxf4nvf4", scale_vec=2),
+              "mxf4nvf4-4x": dict(a_format="e2m1", scaling="ue8m0", kind="mxf4nvf4", scale_vec=4)}
+
+
+@pytest.mark.parametrize("kind", sorted(E2M1_KINDS))
 @pytest.mark.parametrize("sparse", [False, True])
-def test_nvfp4_kernel_regime_boundaries(sparse):
-    rng = np.random.Generator(np.random.PCG64(4242 + sparse))
+def test_e2m1_kernels_regime_boundaries(kind, sparse):
+    """The NVFP4 and MXF4-family kernels on adversarial scales, C words and
+    (sparse) illegal selectors, against the oracle and the generic kernel."""
+    rng = np.random.Generator(np.random.PCG64(4242 + sparse + 10 * sorted(E2M1_KINDS).index(kind)))
     n = 1 << 16
     a, b, c, sa, sb, meta = _nvfp4_adversarial(rng, n, sparse)
-    kw = dict(a_format="e2m1", scaling="ue4m3", scale_vec=4)
+    kw = E2M1_KINDS[kind]
     want, st = oracle.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta, **kw)
     ok = st == 0
     assert ok.any()
     got = t5.mma_dot_batch(a[ok], b[ok], c[ok], scale_a=sa[ok], scale_b=sb[ok],
                            sparse_metadata=None if meta is None else meta[ok], **kw)
-    assert_words_equal(got, want[ok], f"nvfp4 sparse={sparse}")
+    assert_words_equal(got, want[ok], f"{kind} sparse={sparse}")
     if sparse:
         # the illegal selectors raise the reference's ValueError, as the generic kernel does
         bad = int(np.flatnonzero(~ok)[0])
@@ -455,7 +464,72 @@ def test_nvfp4_kernel_regime_boundaries(sparse):
         fast = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta, check=False, **kw)
         generic = t5.mma_dot_batch(a, b, c, scale_a=sa, scale_b=sb, sparse_metadata=meta, check=False,
                                    generic=True, **kw)
-        assert_words_equal(fast, generic, "nvfp4 sparse fast vs generic (illegal selectors included)")
+        assert_words_equal(fast, generic, f"{kind} sparse fast vs generic (illegal selectors included)")
+
+
+@pytest.fixture(scope="module")
+def golden_boundaries():
+    import json
+
+    from conftest import GOLDEN
+
+    return json.loads((GOLDEN / "boundaries.json").read_text()), dict(np.load(GOLDEN / "boundaries.npz"))
+
+
+def _compressed_device_inputs(cases):
+    """The kernels' own layout of scaled E2M1 cases on the device: A packed
+    at physical K (only the selected elements, for sparse cases), B at
+    logical K, and scale rows cut to the blocks the 64 physical elements
+    reach (two bytes for 32-wide blocks)."""
+    import torch
+
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import packing
+
+    dev = torch.device("cuda")
+    a = cases.a
+    if cases.meta is not None:
+        a = a[workloads.active_mask(cases.meta, cases.k, "4of8")].reshape(cases.n, 64)
+    d = full_desc(cases.desc)
+    blocks = 4 if (d["scaling"] == "ue4m3" or d["scale_vec"] == 4) else 2
+    pa = t5.PackedRows(torch.from_numpy(packing.pack_rows(a, nat.FMT_E2M1)).to(dev), a.shape[1],
+                       compressed=cases.meta is not None)
+    pb = t5.PackedRows(torch.from_numpy(packing.pack_rows(cases.b, nat.FMT_E2M1)).to(dev), cases.k)
+    kw = dict(scale_a=torch.from_numpy(np.ascontiguousarray(cases.scale_a[:, :blocks])).to(dev),
+              scale_b=torch.from_numpy(np.ascontiguousarray(cases.scale_b[:, :blocks])).to(dev))
+    if cases.meta is not None:
+        kw["sparse_metadata"] = torch.from_numpy(cases.meta.view(np.int32)).to(dev)
+    return pa, pb, torch.from_numpy(cases.c.view(np.int32)).to(dev), kw
+
+
+@pytest.mark.parametrize("kind,sparse,floor", workloads.BOUNDARY_SETS)
+def test_boundary_sets_match_reference_words(kind, sparse, floor, golden_boundaries):
+    """The regime-boundary sets (C band, truncating groups, the 2**-174
+    floor, NaN scales) word for word against the reference's outputs:
+    host words through the public API, the kernels' compressed device
+    layout with the scale rows cut to the reached blocks, and the generic
+    kernel."""
+    index, arrays = golden_boundaries
+    cases = workloads.boundary_cases(kind, index["cases"], index["seed"], sparse=sparse, floor=floor)
+    assert cases.digest() == index["sets"][cases.name]["sha256"]
+    want = arrays[cases.name]
+    assert_words_equal(gpu_cases(cases), want, cases.name)
+    assert_words_equal(gpu_cases(cases, generic=True), want, cases.name + " (generic kernel)")
+    d = full_desc(cases.desc)
+    pa, pb, c, kw = _compressed_device_inputs(cases)
+    got = t5.mma_dot_batch(pa, pb, c, **{k: d[k] for k in KEYS}, **kw)
+    assert_words_equal(got.cpu().numpy(), want, cases.name + " (compressed device layout)")
+
+
+@pytest.mark.parametrize("kind,sparse,floor", workloads.BOUNDARY_SETS)
+def test_boundary_sets_fresh_seed_match_oracle(kind, sparse, floor):
+    cases = workloads.boundary_cases(kind, 1 << 17, 99, sparse=sparse, floor=floor)
+    want = oracle.eval_cases(cases)
+    assert_words_equal(gpu_cases(cases), want, cases.name)
+    d = full_desc(cases.desc)
+    pa, pb, c, kw = _compressed_device_inputs(cases)
+    got = t5.mma_dot_batch(pa, pb, c, **{k: d[k] for k in KEYS}, **kw)
+    assert_words_equal(got.cpu().numpy(), want, cases.name + " (compressed device layout)")
 
 
 @pytest.mark.parametrize("name", ["e4m3xe5m2-k32", "e4m3xe5m2-k32-f16", "nvfp4-k64", "nvfp4-sparse-k128",
