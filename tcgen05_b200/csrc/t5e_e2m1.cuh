@@ -12,22 +12,17 @@
 
 #include <cstdint>
 
+#include "t5e_select.cuh"
+
 namespace t5e {
 namespace e2m1 {
+
+using namespace select;
 
 constexpr uint32_t kMag0 = 0x03020100u;  // |n| of magnitude codes 0-3 (units of 2**-1)
 constexpr uint32_t kMag1 = 0x0C080604u;  // |n| of magnitude codes 4-7
 constexpr uint32_t kRaw0 = 0x04040400u;  // 0 for code 0, else raw exponent + 4 (codes 0-3)
 constexpr uint32_t kRaw1 = 0x06060505u;  // codes 4-7
-
-// PTX byte permute in its default mode: a selector nibble with bit 3 set
-// yields the sign (bit 7) of the selected byte replicated, i.e. 0x00 for the
-// tables above, whose bytes are all below 0x80.
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
-}
 
 // x >> 16 on the multiply pipe (the ALU pipe is this kernel's bottleneck).
 __device__ __forceinline__ uint32_t hi16(uint32_t x) {
@@ -78,44 +73,6 @@ __device__ __forceinline__ bool block_exceeds(uint32_t wa0, uint32_t wa1, uint32
   acc |= (prmt(kRaw0, kRaw1, a1) + prmt(kRaw0, kRaw1, b1) + bias);
   acc |= (prmt(kRaw0, kRaw1, a1 >> 16) + prmt(kRaw0, kRaw1, b1 >> 16) + bias);
   return (acc & 0x80808080u) != 0u;
-}
-
-// Metadata word (eight 4:8 chunk selectors) -> byte-permute selectors for
-// the four physical words it produces (two chunks each), or false when a
-// selector is illegal.  Selector 6 picks the same pairs as 9 and is
-// rewritten to it; afterwards a legal selector has its first pair index
-// below its second (simulator.py:9-10, :66-67).
-__device__ __forceinline__ bool chunk_selectors(uint32_t m, uint32_t& sel_lo, uint32_t& sel_hi) {
-  const uint32_t x = m ^ 0x66666666u;
-  const uint32_t zero = ~(((x & 0x77777777u) + 0x77777777u) | x) & 0x88888888u;
-  m ^= (zero >> 3) * 0xFu;
-  const uint32_t f = m & 0x33333333u, g = (m >> 2) & 0x33333333u;
-  const uint32_t t = (g | 0x44444444u) - f;  // 4 + g - f per nibble, in [1, 7]
-  if (((t + 0x33333333u) & 0x88888888u) != 0x88888888u) return false;
-  // spread the 2-bit pair indices into selector nibbles; the second chunk of
-  // each physical word reads the second source word (byte indices 4-7)
-  auto spread = [](uint32_t v) {
-    v = (v | (v << 8)) & 0x00FF00FFu;
-    v = (v | (v << 4)) & 0x0F0F0F0Fu;
-    v = (v | (v << 2)) & 0x33333333u;
-    return v | 0x44004400u;
-  };
-  sel_lo = spread(m & 0xFFFFu);
-  sel_hi = spread(m >> 16);
-  return true;
-}
-
-// Eight physical words from sixteen logical words of a row.
-__device__ __forceinline__ void select_row(const uint32_t (&lw)[16], uint32_t s0, uint32_t s1, uint32_t s2,
-                                           uint32_t s3, uint32_t (&pw)[8]) {
-  pw[0] = prmt(lw[0], lw[1], s0);
-  pw[1] = prmt(lw[2], lw[3], s0 >> 16);
-  pw[2] = prmt(lw[4], lw[5], s1);
-  pw[3] = prmt(lw[6], lw[7], s1 >> 16);
-  pw[4] = prmt(lw[8], lw[9], s2);
-  pw[5] = prmt(lw[10], lw[11], s2 >> 16);
-  pw[6] = prmt(lw[12], lw[13], s3);
-  pw[7] = prmt(lw[14], lw[15], s3 >> 16);
 }
 
 template <int WORDS>

@@ -603,6 +603,196 @@ def _pipelined_batch(selected, desc, a, b, c, sa, sb, meta, flags, sparse, k, n,
     return out
 
 
+def _raw_words_pinned(x) -> bool:
+    """A pinned host tensor of raw 32-bit container words, [N, K]."""
+    import torch
+
+    return _pinned(x) and x.dim() == 2 and x.dtype in (torch.int32, torch.uint32)
+
+
+def _pack_chunk(raw, fmt: int, out, stream) -> None:
+    """Raw words already on the device -> packed rows in ``out`` (t5e_pack_rows)."""
+    rc = nat.load().t5e_pack_rows(fmt, raw.data_ptr(), raw.shape[0], raw.shape[1], out.data_ptr(), out.shape[1],
+                                  ctypes.c_void_p(stream.cuda_stream))
+    nat.check(rc, "t5e_pack_rows")
+
+
+def _streamed_words(parts, n: int, dev, out, wait: bool, launch, chunks: int, align: int = 1024):
+    """Raw container words in pinned host memory, streamed through the GPU:
+    each chunk of cases is copied up as raw words on the upload stream,
+    packed into the kernels' row layout on the device (t5e_pack_rows) and
+    evaluated on the current stream once its copy has landed, and its result
+    words are copied down on the download stream, so that the copies of one
+    chunk overlap the packing and evaluation of the others.
+
+    ``parts`` maps a name to (host tensor, rows per case, pack format or
+    None): a part has ``per`` = (num, den) rows for each case (a fraction
+    for rows shared by the cases of a tile).  ``launch(dev_parts, d_dev, s0, s1)`` evaluates
+    cases [s0, s1) on the current stream from the device copies (packed rows
+    for the parts with a format, raw words for the others) into ``d_dev``.
+    Chunks hold whole multiples of ``align`` cases.  Returns ``out`` when
+    ``wait``, else a PendingBatch holding every buffer until its download has
+    finished."""
+    import torch
+
+    comp = torch.cuda.current_stream(dev)
+    up, down = _copy_streams(dev)
+    raw = {name: torch.empty(h.shape, dtype=h.dtype, device=dev) for name, (h, _, _) in parts.items()}
+    packed = {name: torch.empty((h.shape[0], packing.row_stride(fmt, h.shape[1])), dtype=torch.uint8, device=dev)
+              for name, (h, _, fmt) in parts.items() if fmt is not None}
+    d_dev = torch.empty(out.shape, dtype=torch.int32, device=dev)
+    up.wait_stream(comp)  # the buffers above come from the allocator on the current stream
+    step = -(-n // chunks)
+    step = (step + align - 1) // align * align
+    for s0 in range(0, n, step):
+        s1 = min(n, s0 + step)
+        with torch.cuda.stream(up):
+            for name, (h, per, _) in parts.items():
+                r0, r1 = _rows(s0, per), _rows(s1, per)
+                raw[name][r0:r1].copy_(h[r0:r1], non_blocking=True)
+            landed = torch.cuda.Event()
+            landed.record(up)
+        comp.wait_event(landed)
+        for name, (h, per, fmt) in parts.items():
+            if fmt is not None:
+                r0, r1 = _rows(s0, per), _rows(s1, per)
+                _pack_chunk(raw[name][r0:r1], fmt, packed[name][r0:r1], comp)
+        launch({**raw, **packed}, d_dev, s0, s1)
+        done = torch.cuda.Event()
+        done.record(comp)
+        down.wait_event(done)
+        with torch.cuda.stream(down):
+            out.view(-1)[s0:s1].copy_(d_dev.view(-1)[s0:s1].view(out.dtype), non_blocking=True)
+    finished = torch.cuda.Event()
+    finished.record(down)
+    # the pinned inputs are read by copies on the upload stream that the
+    # pinned-memory allocator does not see: they stay referenced until the
+    # batch has finished, with the device buffers
+    keep = (raw, packed, d_dev, {name: h for name, (h, _, _) in parts.items()})
+    if not wait:
+        return PendingBatch(out, finished, keep)
+    finished.synchronize()
+    return out
+
+
+def _words_batch(selected, desc, a, b, c, scale_a, scale_b, sparse_metadata, a_format, scaling, kind, dev, out,
+                 check, generic, wait):
+    """mma_dot_batch on raw container words in pinned host memory (every
+    per-case array pinned): streamed through the GPU by _streamed_words, the
+    operand rows packed on the device."""
+    import torch
+
+    n, k = a.shape
+    if b.shape != (n, k):
+        raise ValueError("A and B dot-product vectors must have equal length")
+    if k > nat.MAX_K:
+        raise ValueError(f"K={k} exceeds the emulator's maximum of {nat.MAX_K}")
+    f16 = desc.d_type == nat.D_F16
+    if c is None or not (_pinned(c) and c.numel() == n and c.element_size() == (2 if f16 else 4)):
+        raise ValueError("streamed raw words need C as a pinned tensor of N words of the C/D type's width")
+    sparse, meta, flags = _prepare(selected, a_format, scaling, kind, k, n, sparse_metadata)
+    per_case_meta = meta is not None and not (flags & nat.FLAG_META_BROADCAST)
+    if per_case_meta and not _pinned(meta):
+        raise ValueError("streamed raw words need per-case metadata in pinned memory")
+    one = (1, 1)
+    parts = {"a": (a, one, desc.a_format), "b": (b, one, desc.b_format), "c": (c.reshape(n), one, None)}
+    scaled = desc.family in (nat.FAMILY_NVFP4, nat.FAMILY_BLOCK_SCALED) and scale_a is not None
+    if scaled:
+        if not (_pinned(scale_a) and _pinned(scale_b) and scale_a.dim() == 2 and scale_a.shape == scale_b.shape):
+            raise ValueError("streamed raw words need [N, blocks] scales in pinned memory")
+        if sparse == 0 and scale_a.shape[1] * desc.scale_block < k:
+            raise ValueError(selected._scale_cover_error)
+        parts["sa"] = (scale_a.view(torch.uint8), one, None)
+        parts["sb"] = (scale_b.view(torch.uint8), one, None)
+    if per_case_meta:
+        parts["meta"] = (meta.view(torch.int32), one, None)
+    shared_meta = None if meta is None or per_case_meta else runtime.to_device(meta, dev, torch.int32)
+    check = check and sparse != 0
+    st_dev = torch.empty(n, dtype=torch.uint8, device=dev) if check else None
+    st_host = torch.empty(n, dtype=torch.uint8, pin_memory=True) if check else None
+    lib = nat.load()
+    fn = lib.t5e_mma_dot_batch_generic if generic else lib.t5e_mma_dot_batch
+    handle = ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def launch(dp, d_dev, s0, s1):
+        db = runtime.DeviceBatch(n=s1 - s0, k=k, a=dp["a"][s0:s1], b=dp["b"][s0:s1], c=dp["c"][s0:s1],
+                                 sparse=sparse, flags=flags)
+        if scaled:
+            db.scale_a, db.scale_b = dp["sa"][s0:s1], dp["sb"][s0:s1]
+        if meta is not None:
+            db.metadata = dp["meta"][s0:s1] if per_case_meta else shared_meta
+        bs = runtime.make_batch_struct(db, d_dev[s0:s1], None if st_dev is None else st_dev[s0:s1])
+        nat.check(fn(ctypes.byref(desc), ctypes.byref(bs), handle), "t5e_mma_dot_batch")
+        if st_dev is not None:
+            down = _copy_streams(dev)[1]
+            ev = torch.cuda.Event()
+            ev.record(torch.cuda.current_stream(dev))
+            down.wait_event(ev)
+            with torch.cuda.stream(down):
+                st_host[s0:s1].copy_(st_dev[s0:s1], non_blocking=True)
+
+    chunks = PIPELINE_CHUNKS if wait or check else PIPELINE_CHUNKS_IN_FLIGHT
+    res = _streamed_words(parts, n, dev, out, wait or check, launch, chunks)
+    if check:
+        st_np = st_host.numpy()
+        if st_np.any():
+            first = int(np.flatnonzero(st_np)[0])
+
+            def meta_error() -> None:
+                record = meta[0] if meta.shape[0] == 1 else meta[first]
+                words = np.asarray(record.cpu() if _is_torch(record) else record).astype(np.int64).tolist()
+                sparse_active_indices(a_format, k, words[0] if flags & nat.FLAG_META_REPEAT else words,
+                                      kind="nvfp4" if (scaling or "").lower() == "ue4m3" else kind)
+
+            _raise_case_status(selected, int(st_np[first]), meta_message=meta_error)
+    return res
+
+
+def _words_tiles(selected, desc, a, b, c, dev, out, generic, wait):
+    """mma_batch on raw words in pinned host memory: tiles streamed through
+    the GPU by _streamed_words, whole tiles per chunk; each chunk's B is
+    transposed on the device (the kernels read B by columns) and packed."""
+    import torch
+
+    t, m, k = a.shape
+    n = b.shape[2]
+    if b.shape[:2] != (t, k):
+        raise ValueError(f"A is {m}x{k} but B has {b.shape[1]} rows")
+    if k > nat.MAX_K:
+        raise ValueError(f"K={k} exceeds the emulator's maximum of {nat.MAX_K}")
+    f16 = desc.d_type == nat.D_F16
+    total = t * m * n
+    if c.numel() != total or c.element_size() != (2 if f16 else 4) or tuple(out.shape) != (t, m, n) \
+            or out.element_size() != 4:
+        raise ValueError("streamed tiles need C and out as pinned [T, M, N] words")
+    per_tile = m * n
+    parts = {"a": (a.reshape(t * m, k), (1, n), desc.a_format), "b": (b.reshape(t * k, n), (k, per_tile), None),
+             "c": (c.reshape(total), (1, 1), None)}
+    lib = nat.load()
+    fn = lib.t5e_mma_dot_batch_generic if generic else lib.t5e_mma_dot_batch
+    comp = torch.cuda.current_stream(dev)
+    handle = ctypes.c_void_p(comp.cuda_stream)
+
+    def launch(dp, d_dev, s0, s1):
+        t0, t1 = s0 // per_tile, s1 // per_tile
+        cols = dp["b"][t0 * k:t1 * k].view(t1 - t0, k, n).transpose(1, 2).contiguous().view((t1 - t0) * n, k)
+        b_rows = torch.empty(((t1 - t0) * n, packing.row_stride(desc.b_format, k)), dtype=torch.uint8, device=dev)
+        _pack_chunk(cols, desc.b_format, b_rows, comp)
+        db = runtime.DeviceBatch(n=s1 - s0, k=k, a=dp["a"][t0 * m:t1 * m], b=b_rows, c=dp["c"][s0:s1],
+                                 tile_m=m, tile_n=n)
+        bs = runtime.make_batch_struct(db, d_dev.view(-1)[s0:s1], None)
+        nat.check(fn(ctypes.byref(desc), ctypes.byref(bs), handle), "t5e_mma_dot_batch")
+
+    chunks = PIPELINE_CHUNKS if wait else PIPELINE_CHUNKS_IN_FLIGHT
+    return _streamed_words(parts, total, dev, out, wait, launch, chunks, align=per_tile)
+
+
+def _rows(case: int, per) -> int:
+    """First row of a case in an array with ``per`` = (num, den) rows per
+    case (fewer than one for rows shared by the cases of a tile)."""
+    return case * per[0] // per[1]
+
+
 def mma_dot_batch(
     a,
     b,
@@ -665,6 +855,10 @@ def _mma_dot_batch(a, b, c, *, model, a_format, b_format, d_type, saturate, scal
         raise TypeError("model must come from tcgen05_b200.make_model or its model classes")
     desc = selected.descriptor()
     dev = runtime.require_device(device)
+    if (_raw_words_pinned(a) and _raw_words_pinned(b) and out is not None and _pinned(out)
+            and out.element_size() == 4 and out.numel() == a.shape[0] and a.shape[0] >= PIPELINE_MIN_CASES):
+        return _words_batch(selected, desc, a, b, c, scale_a, scale_b, sparse_metadata, a_format, scaling, kind,
+                            dev, out, check, generic, wait)
     host_result = not ((_is_torch(a) and a.is_cuda) or (isinstance(a, PackedRows) and _is_torch(a.data)
                                                         and a.data.is_cuda))
     streamed = (isinstance(a, PackedRows) and isinstance(b, PackedRows) and _pinned(a.data) and _pinned(b.data)
@@ -769,19 +963,33 @@ def mma_batch(
     device=None,
     check: bool = True,
     generic: bool = False,
+    out=None,
+    wait: bool = True,
 ):
     """T independent row-major tiles ``D[t] = A[t] @ B[t] + C[t]`` in one
     launch: ``a`` [T, M, K], ``b`` [T, K, N], ``c`` [T, M, N] raw words;
     ``scale_a`` [T, M, blocks], ``scale_b`` [T, N, blocks]; one metadata
     value shared by all tiles (as ``mma``), or an array of T ints / [T, W]
     words.  Returns [T, M, N] words (numpy for host inputs, torch.uint32 on
-    the device for device inputs)."""
+    the device for device inputs).
+
+    Unscaled dense tiles whose A, B and C are raw words in pinned host
+    memory, with a pinned [T, M, N] ``out`` of 32-bit words, are streamed
+    through the GPU a group of tiles at a time (copies up, packing and
+    evaluation on the device, copies down, overlapped); ``wait=False`` then
+    returns a PendingBatch, as for mma_dot_batch."""
     import torch
 
     selected = model or make_model(a_format, b_format, d_type=d_type, saturate=saturate, scaling=scaling,
                                    scale_vec=scale_vec, kind=kind)
     desc = selected.descriptor()
     dev = runtime.require_device(device)
+    if (_pinned(a) and _pinned(b) and c is not None and _pinned(c) and out is not None and _pinned(out)
+            and a.dim() == 3 and b.dim() == 3 and scale_a is None and sparse_metadata is None
+            and a.dtype in (torch.int32, torch.uint32) and b.dtype in (torch.int32, torch.uint32)):
+        return _words_tiles(selected, desc, a, b, c, dev, out, generic, wait)
+    if out is not None or not wait:
+        raise ValueError("out and wait=False apply to pinned host tiles of raw words (unscaled, dense)")
     on_device = _is_torch(a) and a.is_cuda
     if on_device:
         t, m, k = a.shape

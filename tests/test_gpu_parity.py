@@ -634,6 +634,69 @@ def test_in_flight_batch_survives_dropped_inputs(name):
     assert_words_equal(o.numpy().view(np.uint32), want, name + " in flight with its inputs dropped")
 
 
+def _pinned_words(cases):
+    """A path's cases as pinned host tensors of raw container words."""
+    import torch
+
+    d = full_desc(cases.desc)
+    f16 = d["d_type"] == "f16"
+    pin = lambda x: torch.from_numpy(np.ascontiguousarray(x)).pin_memory()  # noqa: E731
+    kw = {k: d[k] for k in KEYS}
+    if cases.scale_a is not None:
+        kw["scale_a"], kw["scale_b"] = pin(cases.scale_a), pin(cases.scale_b)
+    if cases.meta is not None:
+        kw["sparse_metadata"] = pin(cases.meta.view(np.int32))
+    c = (cases.c & 0xFFFF).astype(np.uint16).view(np.int16) if f16 else cases.c.view(np.int32)
+    return pin(cases.a.view(np.int32)), pin(cases.b.view(np.int32)), pin(c), kw
+
+
+@pytest.mark.parametrize("name", ["dense-tf32", "sparse-bf16", "sparse-fp8", "sparse-mx-e2m3", "dense-mxf4",
+                                  "sparse-mxf4nvf4-4x", "mixed-e2m1-e4m3-f16", "i8-s8-u8-saturate",
+                                  "sparse-nvfp4"])
+def test_raw_words_streamed_from_pinned_memory(name):
+    """Raw container words in pinned host memory take the streamed path
+    (copies up, packing on the device, evaluation, copies down): the words
+    equal the oracle's, waited for or left in flight with the inputs
+    dropped."""
+    import torch
+
+    spec = {s.name: s for s in workloads.validation_paths()}[name]
+    cases = workloads.path_cases(spec, (1 << 17) + 1000, seed=spec.seed + 4040)
+    want = oracle.eval_cases(cases)
+    a, b, c, kw = _pinned_words(cases)
+    out = torch.full((cases.n,), -1, dtype=torch.int32).pin_memory()
+    got = t5.mma_dot_batch(a, b, c, out=out, **kw)
+    assert got is out
+    assert_words_equal(out.numpy().view(np.uint32), want, name + " streamed raw words")
+    out2 = torch.full((cases.n,), -1, dtype=torch.int32).pin_memory()
+    p = t5.mma_dot_batch(a, b, c, out=out2, wait=False, check=False, **kw)
+    del a, b, c, kw
+    assert p.wait() is out2
+    assert_words_equal(out2.numpy().view(np.uint32), want, name + " streamed raw words in flight")
+
+
+def test_raw_word_tiles_streamed_from_pinned_memory():
+    """Matrix tiles of raw words in pinned memory, streamed a group of tiles
+    at a time: equal to the one-launch evaluation of the same tiles."""
+    import torch
+
+    rng = np.random.default_rng(808)
+    t, m, n, k = 40, 128, 256, 16
+    a = workloads.f32_words(rng, t * m * k).reshape(t, m, k)
+    b = workloads.f32_words(rng, t * k * n).reshape(t, k, n)
+    c = workloads.f32_words(rng, t * m * n, finite_only=True).reshape(t, m, n)
+    want = t5.mma_batch(a, b, c, a_format="bf16")
+    pin = lambda x: torch.from_numpy(x.view(np.int32)).pin_memory()  # noqa: E731
+    out = torch.full((t, m, n), -1, dtype=torch.int32).pin_memory()
+    got = t5.mma_batch(pin(a), pin(b), pin(c), a_format="bf16", out=out)
+    assert got is out
+    assert_words_equal(out.numpy().view(np.uint32).reshape(-1), want.reshape(-1), "streamed tiles")
+    out2 = torch.full((t, m, n), -1, dtype=torch.int32).pin_memory()
+    p = t5.mma_batch(pin(a), pin(b), pin(c), a_format="bf16", out=out2, wait=False)
+    assert p.wait() is out2
+    assert_words_equal(out2.numpy().view(np.uint32).reshape(-1), want.reshape(-1), "streamed tiles in flight")
+
+
 @pytest.mark.parametrize("name", ["e4m3xe5m2-k32-f16", "nvfp4-sparse-k128", "u8xs8-k32-wrap"])
 def test_pinned_host_batches_stream_in_chunks(name):
     """Pinned host operands, C and output take the chunked copy/compute
