@@ -250,7 +250,7 @@ def build_step(torch, dev, rank: int, world: int) -> list[Launch]:
         items.append(Launch(spec.name, kernel_of(spec), model.descriptor(), db, d, macs, nbytes, lo))
     t0, t1 = sweep.shard(MATRIX_TILES, rank, world)
     per_tile = TILE_M * TILE_N
-    model, db = workloads.device_config("matrix-bf16", dev, seed=7000 + t0, n=(t1 - t0) * per_tile)
+    model, db = sweep.matrix_tiles(t0, t1 - t0, dev, TILE_M, TILE_N, TILE_K)
     macs, nbytes = workloads.config_work("matrix-bf16", db)
     d = torch.empty(db.n, dtype=torch.int32, device=dev)
     items.append(Launch("matrix-bf16", "wide_tile_kernel", model.descriptor(), db, d, macs, nbytes, t0 * per_tile))
@@ -760,7 +760,8 @@ def report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mis
         "vs_baseline": None,
         "dtype": "u32",
         "data": "synthetic: seeded counter-hash words with the reference harness's distributions "
-                "(tcgen05_b200.sweep; numpy mirror for the host), random BF16 tile words",
+                "(tcgen05_b200.sweep; numpy mirror for the host); uniformly random 32-bit tile words by the same "
+                "hash of the global row and case index",
         "config": {"workload": "46-path validation sweep, 1M cases per path (46M total, sharded), plus matrix mma "
                                "BF16 M=128 N=256 K=16 F32 D, 4096 tiles (sharded)",
                    "cases_per_path": CASES_PER_PATH, "paths": 46, "matrix_tiles": MATRIX_TILES,

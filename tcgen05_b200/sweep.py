@@ -344,6 +344,35 @@ def device_batch(spec: W.PathSpec, start: int, count: int, total: int, device):
     return model, db
 
 
+MATRIX_SEED = 92901  # counter-hash seed of the matrix configuration's tile words
+
+
+def matrix_tiles(first_tile: int, tiles: int, device, m: int = 128, n: int = 256, k: int = 16):
+    """Tiles [first_tile, first_tile + tiles) of the matrix configuration
+    (BF16 A [m x k] and B [k x n] words, F32 C words, uniformly random
+    32-bit patterns, NaN/Inf/subnormals included) on `device` in the
+    kernels' layout: (model, DeviceBatch).  Every word is the counter hash of
+    its global row or case index, so any split of the tiles over GPUs
+    evaluates the same cases.  BF16 rows keep the high half of each word."""
+    import torch
+
+    from .model import make_model
+    from .runtime import DeviceBatch
+
+    def rows(stream, first, count, words):
+        idx = torch.arange(first, first + count, dtype=torch.int64, device=device)
+        h = case_hash(torch, MATRIX_SEED, stream, idx, words)
+        return torch.where(h >= 1 << 31, h - (1 << 32), h).to(torch.int32)
+
+    a = rows(S_A, first_tile * m, tiles * m, k)        # [rows, k] raw words
+    b = rows(S_B, first_tile * n, tiles * n, k)        # [columns, k] raw words (B rows are its columns)
+    c = rows(S_C, first_tile * m * n, tiles * m * n, 1).reshape(-1)
+    pack = lambda w: (w >> 16).to(torch.int16).view(torch.uint8).reshape(w.shape[0], 2 * k)  # noqa: E731
+    db = DeviceBatch(n=tiles * m * n, k=k, a=pack(a).contiguous(), b=pack(b).contiguous(), c=c.contiguous(),
+                     tile_m=m, tile_n=n)
+    return make_model("bf16"), db
+
+
 def path_work(spec: W.PathSpec, cases: int, model=None) -> tuple[int, int]:
     """(element-MACs, algorithmic bytes) of `cases` cases of a path.  MACs are
     the physical products; bytes follow the per-path formula: packed A at
