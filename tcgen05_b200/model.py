@@ -442,23 +442,225 @@ FORMAT_MODELS = {
     "e2m1": Tcgen05RawWindowFp4E2M1MmaModel,
 }
 
-F16_INPUT_FORMATS = frozenset(("bf16", "f16"))
-F8F6F4_INPUT_FORMATS = frozenset(("e4m3", "e5m2", "e2m3", "e3m2", "e2m1"))
+# ------------------------------------------------------- descriptor factory
+#
+# make_model resolves a descriptor in two moves.  A route is chosen from the
+# operand formats and the scale format alone (integer operands; unscaled
+# floating point; UE4M3 scales; one route per UE8M0 kind).  The route is then
+# a list of steps run in order -- checks that reject the descriptor with the
+# reference's message (tcgen05_model/model.py:1185-1309), defaults filled in
+# for omitted keywords, and the inference of the UE8M0 kind -- followed by a
+# builder that returns the model.  The order of the routes' checks is the
+# reference's order of rejection, so the first violated rule names the
+# descriptor's first problem as the reference does; the descriptor grid of
+# tests/golden (944 descriptors generated from the reference) pins it.
+
+_INTEGER = frozenset(("u8", "s8"))
+_HALF = frozenset(("bf16", "f16"))
+_NARROW = frozenset(("e4m3", "e5m2", "e2m3", "e3m2", "e2m1"))
+_ALL_FORMATS = frozenset(("tf32",)) | _HALF | _NARROW | _INTEGER
+_FLOAT_D = ("f16", "f32")
+
+# kept under the reference's names: part of the public surface
+F16_INPUT_FORMATS = _HALF
+F8F6F4_INPUT_FORMATS = _NARROW
+
+_ALIASES = {"fp8": "e4m3", "fp8e4m3": "e4m3", "fp8e5m2": "e5m2", "fp6e2m3": "e2m3", "fp6e3m2": "e3m2",
+            "fp4": "e2m1", "fp4e2m1": "e2m1"}
 
 
 def normalize_format(name: str) -> str:
-    """Canonical short format name (tcgen05_model/model.py:1169-1182)."""
-    normalized = name.lower().replace("_", "").replace("-", "")
-    aliases = {
-        "fp8": "e4m3",
-        "fp8e4m3": "e4m3",
-        "fp8e5m2": "e5m2",
-        "fp6e2m3": "e2m3",
-        "fp6e3m2": "e3m2",
-        "fp4": "e2m1",
-        "fp4e2m1": "e2m1",
-    }
-    return aliases.get(normalized, normalized)
+    """Canonical short format name: lower case without '_' and '-', with the
+    fp8/fp6/fp4 aliases of tcgen05_model/model.py:1169-1182."""
+    key = name.lower().replace("_", "").replace("-", "")
+    return _ALIASES.get(key, key)
+
+
+@dataclass(frozen=True)
+class _Desc:
+    """A descriptor being resolved (formats normalised, lower-case names)."""
+
+    a: str
+    b: str
+    d: str
+    saturate: bool
+    scaling: str | None
+    scale_vec: int | None
+    kind: str | None
+
+    def with_(self, **kw) -> "_Desc":
+        fields = dict(self.__dict__)
+        fields.update(kw)
+        return _Desc(**fields)
+
+
+@dataclass(frozen=True)
+class _Reject:
+    """A check: the descriptor is rejected with `message` (formatted with the
+    descriptor's fields) when `violated` holds."""
+
+    violated: object
+    message: str
+
+    def apply(self, x: _Desc) -> _Desc:
+        if self.violated(x):
+            raise ValueError(self.message.format(**x.__dict__))
+        return x
+
+
+@dataclass(frozen=True)
+class _Default:
+    """An omitted keyword takes its value for the route."""
+
+    field: str
+    value: object
+
+    def apply(self, x: _Desc) -> _Desc:
+        return x if getattr(x, self.field) is not None else x.with_(**{self.field: self.value})
+
+
+@dataclass(frozen=True)
+class _Route:
+    steps: tuple
+    build: object
+
+
+def _uses_block_scaling(x: _Desc) -> bool:
+    return x.scaling is not None or x.kind is not None or x.scale_vec is not None
+
+
+# checks every descriptor passes first
+_FORMAT_CHECKS = (
+    _Reject(lambda x: x.a not in _ALL_FORMATS or x.b not in _ALL_FORMATS,
+            "unsupported input format combination: {a}/{b}"),
+    _Reject(lambda x: x.d not in ("f16", "f32", "s32"), "unsupported C/D type: {d!r}"),
+)
+
+# the instruction an unscaled floating-point descriptor names, and its rules
+_UNSCALED_KINDS = (
+    (lambda x: "tf32" in (x.a, x.b),
+     (_Reject(lambda x: x.a != x.b or x.d != "f32", "kind::tf32 requires TF32 A/B and F32 C/D"),)),
+    (lambda x: x.a in _HALF or x.b in _HALF,
+     (_Reject(lambda x: x.a != x.b or x.a not in _HALF, "B200 kind::f16 requires matching BF16/BF16 or F16/F16 A/B"),
+      _Reject(lambda x: x.d == "f16" and x.a != "f16", "B200 kind::f16 permits F16 C/D only with F16 A/B"),
+      _Reject(lambda x: x.d not in _FLOAT_D, "kind::f16 requires F16 or F32 C/D"))),
+    (lambda x: x.a in _NARROW and x.b in _NARROW,
+     (_Reject(lambda x: x.d not in _FLOAT_D, "kind::f8f6f4 requires F16 or F32 C/D"),)),
+)
+
+@dataclass(frozen=True)
+class _Select:
+    """The first of `options` (test, steps) whose test holds contributes its
+    steps; with none, the descriptor is rejected with `message`."""
+
+    options: tuple
+    message: str
+
+    def apply(self, x: _Desc) -> _Desc:
+        for test, steps in self.options:
+            if test(x):
+                for step in steps:
+                    x = step.apply(x)
+                return x
+        raise ValueError(self.message.format(**x.__dict__))
+
+
+@dataclass(frozen=True)
+class _InferKind:
+    """A UE8M0 descriptor without ``kind`` is MXF8F6F4 when its operands are
+    f8/f6/f4 and not both E2M1; otherwise the kind is ambiguous."""
+
+    def apply(self, x: _Desc) -> _Desc:
+        if x.kind is not None:
+            return x
+        if x.a in _NARROW and x.b in _NARROW and (x.a, x.b) != ("e2m1", "e2m1"):
+            return x.with_(kind="mxf8f6f4")
+        raise ValueError("kind is required for ambiguous UE8M0 descriptors")
+
+
+_MXF8F6F4_SAME = {
+    "e4m3": lambda: Tcgen05BlockScaledMxf8f6f4E4M3MmaModel(),
+    "e5m2": lambda: Tcgen05BlockScaledMxf8f6f4E5M2MmaModel(),
+    "e2m3": lambda: Tcgen05BlockScaledMxf8f6f4E2M3MmaModel(),
+    "e3m2": lambda: Tcgen05BlockScaledMxf8f6f4E3M2MmaModel(),
+    "e2m1": lambda: Tcgen05BlockScaledMxf8f6f4E2M1MmaModel(),
+}
+
+
+def _build_unscaled(x: _Desc):
+    if x.d == "f32" and x.a == x.b and x.a in FORMAT_MODELS:
+        return FORMAT_MODELS[x.a]()
+    return Tcgen05MixedRawWindowMmaModel(x.a, x.b, d_type=x.d)
+
+
+def _build_mxf8f6f4(x: _Desc):
+    if x.a == x.b:
+        return _MXF8F6F4_SAME[x.a]()
+    kw = _mxf8f6f4_kwargs(_tcgen05_decoder_for_format(x.a))
+    kw["input_decoder_b"] = _tcgen05_decoder_for_format(x.b)
+    return Tcgen05BlockScaledMmaModel(**kw)
+
+
+def _both_e2m1(x: _Desc) -> bool:
+    return x.a == "e2m1" and x.b == "e2m1"
+
+
+_ROUTES = {
+    "i8": _Route(
+        (_Reject(_uses_block_scaling, "kind::i8 does not use block scaling"),
+         _Reject(lambda x: x.a not in _INTEGER or x.b not in _INTEGER or x.d != "s32",
+                 "kind::i8 requires U8/S8 A and B with S32 C/D")),
+        lambda x: Tcgen05I8S32MmaModel(a_type=x.a, b_type=x.b, saturate=x.saturate)),
+    "unscaled": _Route(
+        (_Reject(lambda x: x.kind is not None, "kind is only used by block-scaled MMA"),
+         _Reject(lambda x: x.scale_vec is not None, "scale_vec is only used by block-scaled MMA"),
+         _Select(_UNSCALED_KINDS, "unsupported floating-point descriptor: {a}/{b}/{d}")),
+        _build_unscaled),
+    "ue4m3": _Route(
+        (_Reject(lambda x: x.kind not in (None, "nvfp4", "mxf4nvf4"),
+                 "UE4M3 scaling is only valid for the NVFP4 family"),
+         _Default("scale_vec", 4),
+         _Reject(lambda x: not _both_e2m1(x) or x.d != "f32" or x.scale_vec != 4,
+                 "UE4M3 scaling models NVFP4 E2M1/E2M1, F32 D, scale_vec::4X")),
+        lambda x: Tcgen05RawWindowNvfp4MmaModel()),
+    "ue8m0": _Route(
+        (_Reject(lambda x: x.kind not in (None, "mxf8f6f4", "mxf4", "mxf4nvf4"),
+                 "unsupported block-scaled kind: {kind!r}"),
+         _Reject(lambda x: x.d != "f32", "block-scaled model currently supports F32 C/D"),
+         _InferKind()),
+        lambda x: _ROUTES["ue8m0:" + x.kind]),
+    "ue8m0:mxf8f6f4": _Route(
+        (_Default("scale_vec", 1),
+         _Reject(lambda x: x.scale_vec != 1, "MXF8F6F4 UE8M0 requires scale_vec::1X"),
+         _Reject(lambda x: x.a not in _NARROW or x.b not in _NARROW, "MXF8F6F4 requires f8/f6/f4 A and B")),
+        _build_mxf8f6f4),
+    "ue8m0:mxf4": _Route(
+        (_Reject(lambda x: not _both_e2m1(x), "{kind} requires E2M1 A and B"),
+         _Default("scale_vec", 2),
+         _Reject(lambda x: x.scale_vec != 2, "MXF4 UE8M0 requires scale_vec::2X")),
+        lambda x: Tcgen05BlockScaledMxf4E2M1MmaModel()),
+    "ue8m0:mxf4nvf4": _Route(
+        (_Reject(lambda x: not _both_e2m1(x), "{kind} requires E2M1 A and B"),
+         _Default("scale_vec", 2),
+         _Reject(lambda x: x.scale_vec not in (2, 4), "MXF4NVF4 UE8M0 requires scale_vec::2X or scale_vec::4X")),
+        lambda x: (Tcgen05BlockScaledMxf4Nvfp4E2M1Scale2XMmaModel() if x.scale_vec == 2
+                   else Tcgen05BlockScaledMxf4Nvfp4E2M1Scale4XMmaModel())),
+}
+
+
+def _route_of(x: _Desc) -> _Route:
+    """The route a checked descriptor takes: integer operands name kind::i8;
+    floating-point ones go by scale format (saturation belongs to kind::i8
+    alone)."""
+    if x.a in _INTEGER or x.b in _INTEGER:
+        return _ROUTES["i8"]
+    if x.saturate:
+        raise ValueError("saturate is only valid for kind::i8")
+    if x.scaling is None:
+        return _ROUTES["unscaled"]
+    if x.scaling in ("ue4m3", "ue8m0"):
+        return _ROUTES[x.scaling]
+    raise ValueError(f"unsupported scale format: {x.scaling!r}")
 
 
 def make_model(
@@ -472,111 +674,23 @@ def make_model(
     sparse: bool = False,
     kind: str | None = None,
 ) -> ScalarModel:
-    """Model selected by a tcgen05 descriptor, with the reference's legality
-    rules and ValueError messages (tcgen05_model/model.py:1185-1309).
+    """The model a tcgen05 descriptor selects, accepting and rejecting
+    descriptors as the reference does, with its ValueError messages
+    (tcgen05_model/model.py:1185-1309).
 
     ``scaling`` accepts None, "ue8m0" or "ue4m3"; ``kind`` disambiguates the
     E2M1 UE8M0 families ("mxf8f6f4", "mxf4", "mxf4nvf4").  ``sparse`` is
-    accepted and unused, as in the reference.
+    accepted and unused, as in the reference: sparsity is an argument of the
+    evaluation, not of the model.
     """
-    a_format = normalize_format(a_format)
-    b_format = normalize_format(b_format or a_format)
-    d_type = d_type.lower()
-    kind = None if kind is None else kind.lower()
-
-    known_formats = frozenset(("tf32", *F16_INPUT_FORMATS, *F8F6F4_INPUT_FORMATS, "u8", "s8"))
-    if a_format not in known_formats or b_format not in known_formats:
-        raise ValueError(f"unsupported input format combination: {a_format}/{b_format}")
-    if d_type not in ("f16", "f32", "s32"):
-        raise ValueError(f"unsupported C/D type: {d_type!r}")
-
-    if a_format in ("u8", "s8") or b_format in ("u8", "s8"):
-        if scaling is not None or kind is not None or scale_vec is not None:
-            raise ValueError("kind::i8 does not use block scaling")
-        if a_format not in ("u8", "s8") or b_format not in ("u8", "s8") or d_type != "s32":
-            raise ValueError("kind::i8 requires U8/S8 A and B with S32 C/D")
-        return Tcgen05I8S32MmaModel(a_type=a_format, b_type=b_format, saturate=saturate)
-
-    if saturate:
-        raise ValueError("saturate is only valid for kind::i8")
-
-    if scaling is None:
-        if kind is not None:
-            raise ValueError("kind is only used by block-scaled MMA")
-        if scale_vec is not None:
-            raise ValueError("scale_vec is only used by block-scaled MMA")
-        if a_format == "tf32" or b_format == "tf32":
-            if a_format != "tf32" or b_format != "tf32" or d_type != "f32":
-                raise ValueError("kind::tf32 requires TF32 A/B and F32 C/D")
-        elif a_format in F16_INPUT_FORMATS or b_format in F16_INPUT_FORMATS:
-            if a_format != b_format or a_format not in F16_INPUT_FORMATS:
-                raise ValueError("B200 kind::f16 requires matching BF16/BF16 or F16/F16 A/B")
-            if d_type == "f16" and a_format != "f16":
-                raise ValueError("B200 kind::f16 permits F16 C/D only with F16 A/B")
-            if d_type not in ("f16", "f32"):
-                raise ValueError("kind::f16 requires F16 or F32 C/D")
-        elif a_format in F8F6F4_INPUT_FORMATS and b_format in F8F6F4_INPUT_FORMATS:
-            if d_type not in ("f16", "f32"):
-                raise ValueError("kind::f8f6f4 requires F16 or F32 C/D")
-        else:
-            raise ValueError(f"unsupported floating-point descriptor: {a_format}/{b_format}/{d_type}")
-        if d_type == "f32" and a_format == b_format and a_format in FORMAT_MODELS:
-            return FORMAT_MODELS[a_format]()
-        return Tcgen05MixedRawWindowMmaModel(a_format, b_format, d_type=d_type)
-
-    scaling = scaling.lower()
-    if scaling == "ue4m3":
-        if kind not in (None, "nvfp4", "mxf4nvf4"):
-            raise ValueError("UE4M3 scaling is only valid for the NVFP4 family")
-        scale_vec = 4 if scale_vec is None else scale_vec
-        if a_format != "e2m1" or b_format != "e2m1" or d_type != "f32" or scale_vec != 4:
-            raise ValueError("UE4M3 scaling models NVFP4 E2M1/E2M1, F32 D, scale_vec::4X")
-        return Tcgen05RawWindowNvfp4MmaModel()
-
-    if scaling != "ue8m0":
-        raise ValueError(f"unsupported scale format: {scaling!r}")
-    if kind not in (None, "mxf8f6f4", "mxf4", "mxf4nvf4"):
-        raise ValueError(f"unsupported block-scaled kind: {kind!r}")
-    if d_type != "f32":
-        raise ValueError("block-scaled model currently supports F32 C/D")
-    if kind is None:
-        if (
-            a_format in F8F6F4_INPUT_FORMATS
-            and b_format in F8F6F4_INPUT_FORMATS
-            and (a_format != "e2m1" or b_format != "e2m1")
-        ):
-            kind = "mxf8f6f4"
-        else:
-            raise ValueError("kind is required for ambiguous UE8M0 descriptors")
-    if kind == "mxf8f6f4":
-        scale_vec = 1 if scale_vec is None else scale_vec
-        if scale_vec != 1:
-            raise ValueError("MXF8F6F4 UE8M0 requires scale_vec::1X")
-        if a_format not in F8F6F4_INPUT_FORMATS or b_format not in F8F6F4_INPUT_FORMATS:
-            raise ValueError("MXF8F6F4 requires f8/f6/f4 A and B")
-        classes = {
-            "e4m3": Tcgen05BlockScaledMxf8f6f4E4M3MmaModel,
-            "e5m2": Tcgen05BlockScaledMxf8f6f4E5M2MmaModel,
-            "e2m3": Tcgen05BlockScaledMxf8f6f4E2M3MmaModel,
-            "e3m2": Tcgen05BlockScaledMxf8f6f4E3M2MmaModel,
-            "e2m1": Tcgen05BlockScaledMxf8f6f4E2M1MmaModel,
-        }
-        if a_format != b_format or a_format not in classes:
-            kw = _mxf8f6f4_kwargs(_tcgen05_decoder_for_format(a_format))
-            kw["input_decoder_b"] = _tcgen05_decoder_for_format(b_format)
-            return Tcgen05BlockScaledMmaModel(**kw)
-        return classes[a_format]()
-    if kind in ("mxf4", "mxf4nvf4"):
-        if a_format != "e2m1" or b_format != "e2m1":
-            raise ValueError(f"{kind} requires E2M1 A and B")
-        scale_vec = 2 if scale_vec is None else scale_vec
-        if kind == "mxf4":
-            if scale_vec != 2:
-                raise ValueError("MXF4 UE8M0 requires scale_vec::2X")
-            return Tcgen05BlockScaledMxf4E2M1MmaModel()
-        if scale_vec == 2:
-            return Tcgen05BlockScaledMxf4Nvfp4E2M1Scale2XMmaModel()
-        if scale_vec == 4:
-            return Tcgen05BlockScaledMxf4Nvfp4E2M1Scale4XMmaModel()
-        raise ValueError("MXF4NVF4 UE8M0 requires scale_vec::2X or scale_vec::4X")
-    raise ValueError(f"unsupported block-scaled descriptor: {kind}/{a_format}/{b_format}")
+    x = _Desc(a=normalize_format(a_format), b=normalize_format(b_format or a_format), d=d_type.lower(),
+              saturate=saturate, scaling=None if scaling is None else scaling.lower(), scale_vec=scale_vec,
+              kind=None if kind is None else kind.lower())
+    for step in _FORMAT_CHECKS:
+        x = step.apply(x)
+    target = _route_of(x)
+    while isinstance(target, _Route):
+        for step in target.steps:
+            x = step.apply(x)
+        target = target.build(x)
+    return target
