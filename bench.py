@@ -51,12 +51,12 @@ sys.path.insert(0, str(REPO))
 
 METRIC = "emulated element-MACs/s (bit-exact) at 1/2/4/8 B200 vs Python model on host"
 UNIT = "element-MACs/s"
-CASES_PER_PATH = 1_000_000
-MATRIX_TILES = 4096
-TILE_M, TILE_N, TILE_K = 128, 256, 16
 NVFP4_CASES = 1 << 24
 E2E_RUNS = 3
 REF_DIR = REPO / "baseline" / "_ref"
+
+from tcgen05_b200.step import (CASES_PER_PATH, MATRIX_TILES, TILE_K, TILE_M, TILE_N,  # noqa: E402
+                               build_step, launcher, whole_step_macs)
 
 
 def measured_peaks() -> tuple[dict, str]:
@@ -123,7 +123,7 @@ def issue_peaks(torch, lib, stream, iters: int = 256, launches: int = 5) -> dict
 
     handle = ctypes.c_void_p(stream.cuda_stream)
     out = {}
-    for pipe, name in ((0, "alu"), (1, "fma")):
+    for pipe, name in ((0, "alu"), (1, "fma"), (2, "fp64")):
         count = ctypes.c_uint64(0)
         for _ in range(2):
             nat.check(lib.t5e_issue_probe(pipe, iters, ctypes.byref(count), handle), "t5e_issue_probe")
@@ -202,73 +202,6 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------- the step
-
-
-def kernel_of(spec) -> str:
-    """The specialised kernel t5e_mma_dot_batch dispatches a path to."""
-    d = spec.descriptor
-    fam, fmt = spec.family, d["a_format"]
-    if fam == "i8":
-        return "i8_kernel"
-    if d["scaling"] == "ue4m3":
-        return "nvfp4_kernel"
-    if fam in ("fp4block", "sparse-fp4block"):
-        return "mxf4_kernel"
-    if fmt in ("tf32", "bf16", "f16") or (fam == "sparse" and spec.params[0] in ("tf32", "bf16", "f16")):
-        return "wide_kernel"
-    if fam in ("mx", "sparse-mx") and fmt in ("e2m3", "e3m2", "e2m1"):
-        return "mx_kernel"
-    return "raw_window_kernel"
-
-
-class Launch:
-    """One launch of the step: a path's shard or the matrix tiles' shard,
-    resident in HBM with its output buffer and the batch struct that
-    t5e_mma_dot_batch takes."""
-
-    def __init__(self, name, kernel, desc, db, d, macs, nbytes, first_case):
-        from tcgen05_b200 import runtime
-
-        self.name, self.kernel, self.desc = name, kernel, desc
-        self.db, self.d = db, d
-        self.struct = runtime.make_batch_struct(db, d, None)
-        self.macs, self.bytes = macs, nbytes
-        self.first_case = first_case  # global index of this shard's first case
-
-
-def build_step(torch, dev, rank: int, world: int) -> list[Launch]:
-    """This rank's shard of every path and of the matrix tiles, generated in
-    HBM in the kernels' layout."""
-    from tcgen05_b200 import sweep, workloads
-
-    items = []
-    lo, hi = sweep.shard(CASES_PER_PATH, rank, world)
-    for spec in workloads.validation_paths():
-        model, db = sweep.device_batch(spec, lo, hi - lo, CASES_PER_PATH, dev)
-        macs, nbytes = sweep.path_work(spec, db.n, model)
-        d = torch.empty(db.n, dtype=torch.int32, device=dev)
-        items.append(Launch(spec.name, kernel_of(spec), model.descriptor(), db, d, macs, nbytes, lo))
-    t0, t1 = sweep.shard(MATRIX_TILES, rank, world)
-    per_tile = TILE_M * TILE_N
-    model, db = sweep.matrix_tiles(t0, t1 - t0, dev, TILE_M, TILE_N, TILE_K)
-    macs, nbytes = workloads.config_work("matrix-bf16", db)
-    d = torch.empty(db.n, dtype=torch.int32, device=dev)
-    items.append(Launch("matrix-bf16", "wide_tile_kernel", model.descriptor(), db, d, macs, nbytes, t0 * per_tile))
-    torch.cuda.synchronize(dev)
-    return items
-
-
-def launcher(lib, stream):
-    from tcgen05_b200 import _native as nat
-
-    handle = ctypes.c_void_p(stream.cuda_stream)
-
-    def launch(item):
-        rc = lib.t5e_mma_dot_batch(ctypes.byref(item.desc), ctypes.byref(item.struct), handle)
-        if rc != 0:
-            nat.check(rc, "t5e_mma_dot_batch " + item.name)
-
-    return launch
 
 
 def per_launch_times(torch, stream, items, launch, steps: int = 3) -> list[float]:
@@ -604,15 +537,6 @@ def port_rate(tasks) -> tuple[float, int]:
 # --------------------------------------------------------------- our arm
 
 
-def whole_step_macs() -> int:
-    """Element-MACs of one step of the whole job: physical products of the
-    46 paths at CASES_PER_PATH cases each, plus the matrix tiles."""
-    from tcgen05_b200 import sweep, workloads
-
-    macs = sum(sweep.path_work(s, CASES_PER_PATH)[0] for s in workloads.validation_paths())
-    return macs + MATRIX_TILES * TILE_M * TILE_N * TILE_K
-
-
 def run_ours(args) -> int:
     import torch
     import torch.distributed as dist
@@ -731,12 +655,15 @@ def report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mis
     achieved = di.bytes / (dms / 1e3) / 1e9
     tag = f"{di.kernel} {di.name}"
     traffic, traffic_state = profiled_figure("traffic_bytes_per_launch", tag, di.kernel)
+    if traffic is not None:
+        traffic /= world  # the ncu figure is for the full configuration on one GPU; a shard moves 1/N of it
     peak_issue = issue_peaks(torch, lib, stream)
     int_pipe = {"alu_peak_warp_inst_per_s": peak_issue["alu"], "fma_peak_warp_inst_per_s": peak_issue["fma"],
+                "fp64_peak_warp_inst_per_s": peak_issue["fp64"],
                 "source": "peaks: t5e_issue_probe in this run; kernel warp instructions per launch: the committed "
                           "ncu summary, used only while its source stamp matches the kernel's source"}
     fracs = {"hbm": achieved / hbm}
-    for pipe in ("alu", "fma"):
+    for pipe in ("alu", "fma", "fp64"):
         per_launch, state = profiled_figure(f"{pipe}_warp_inst_per_launch", tag, di.kernel)
         int_pipe[f"kernel_{pipe}_warp_inst_per_launch"] = per_launch
         int_pipe[f"{pipe}_figure"] = state

@@ -232,7 +232,8 @@ int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch* host, voi
 /* Integer issue-rate probe, a measurement helper for the integer roofline
  * (no counterpart in the reference).  Launches on `stream` two blocks of 1024
  * threads per SM that issue nothing but independent chains of one pipe's
- * instructions: pipe 0 the ALU pipe (LOP3, SHF), pipe 1 the FMA pipe (IMAD);
+ * instructions: pipe 0 the ALU pipe (LOP3, SHF), pipe 1 the FMA pipe (IMAD),
+ * pipe 2 the FP64 pipe (DFMA);
  * `iters` (1..2^20) loop iterations of 256 such instructions per
  * thread.  Stores the number of those warp instructions the launch issues in
  * *warp_instructions; timed with events on `stream`, it gives the pipe's

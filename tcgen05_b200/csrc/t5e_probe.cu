@@ -2,7 +2,8 @@
 //
 // The emulator kernels are integer work on the ALU pipe (LOP3, SHF, PRMT,
 // IMNMX, ...) and the FMA pipe (IMAD, IMUL; the assembler also issues 32-bit
-// adds there), not tensor-core work, so their
+// adds there), and for the matrix tiles exact FP64 work (DFMA, DADD), not
+// tensor-core work, so their
 // compute roofline is the issue rate of those pipes at the SM clock the GPU
 // runs at.  No vendor figure states it for this part, so it is measured:
 // these kernels issue nothing but independent chains of one pipe's
@@ -66,6 +67,33 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) issue_kernel(uint32_t 
   if (acc == 0x2545F491u && seed == 0x68E31DA4u) g_sink[blockIdx.x & 1023u] = acc;
 }
 
+// FP64 pipe: DFMA chains, the pipe the matrix tile kernel forms and
+// truncates its terms on.  Values stay near 1 (x*p + q with p, q in
+// [0.25, 0.75)), so no chain reaches a special value.
+__global__ void __launch_bounds__(kThreads, kBlocksPerSm) issue_kernel_fp64(uint32_t iters, uint32_t seed) {
+  double x[kChains];
+#pragma unroll
+  for (int c = 0; c < kChains; ++c)
+    x[c] = 0.25 + 0.5 * (double)(((seed + 0x9E3779B9u * (uint32_t)(c + 1)) ^ threadIdx.x) & 0xFFFFu) / 65536.0;
+  for (uint32_t it = 0; it < iters; ++it) {
+#pragma unroll
+    for (int s = 0; s < kSteps; ++s) {
+      double y[kChains];
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) {
+        const double p = 0.25 + 0.5 * x[(c + 1) % kChains], q = 0.25 * x[(c + 3) % kChains];
+        asm volatile("fma.rn.f64 %0, %1, %2, %3;" : "=d"(y[c]) : "d"(x[c]), "d"(p), "d"(q));
+      }
+#pragma unroll
+      for (int c = 0; c < kChains; ++c) x[c] = y[c];
+    }
+  }
+  double acc = 0.0;
+#pragma unroll
+  for (int c = 0; c < kChains; ++c) acc += x[c];
+  if (acc == 1234.5 && seed == 0x68E31DA4u) g_sink[blockIdx.x & 1023u] = (uint32_t)acc;
+}
+
 }  // namespace probe
 }  // namespace t5e
 
@@ -73,7 +101,7 @@ using namespace t5e;
 
 extern "C" int t5e_issue_probe(int32_t pipe, uint32_t iters, uint64_t* warp_instructions, void* stream) {
   using namespace t5e::probe;
-  if ((pipe != 0 && pipe != 1) || iters < 1 || iters > kMaxIters || !warp_instructions) return T5E_ERR_INVALID;
+  if (pipe < 0 || pipe > 2 || iters < 1 || iters > kMaxIters || !warp_instructions) return T5E_ERR_INVALID;
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -85,7 +113,8 @@ extern "C" int t5e_issue_probe(int32_t pipe, uint32_t iters, uint64_t* warp_inst
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // the mix of the ALU probe: in each step, even chains LOP3, odd chains SHF
   if (pipe == 0) issue_kernel<0><<<grid, kThreads, 0, s>>>(iters, 0x1234567u);
-  else issue_kernel<1><<<grid, kThreads, 0, s>>>(iters, 0x1234567u);
+  else if (pipe == 1) issue_kernel<1><<<grid, kThreads, 0, s>>>(iters, 0x1234567u);
+  else issue_kernel_fp64<<<grid, kThreads, 0, s>>>(iters, 0x1234567u);
   const int rc = kernel_status("t5e_issue_probe launch");
   if (rc != T5E_OK) return rc;
   *warp_instructions = (uint64_t)grid * (kThreads / 32) * iters * kSteps * kChains;

@@ -1,0 +1,124 @@
+"""One step of the benchmark workload, resident in HBM: the 46-path
+validation sweep at 1M cases per path plus the matrix configuration (4,096
+BF16 tiles of 128 x 256 x 16), sharded over the ranks of a job.
+
+``build_step`` generates a rank's shard of every path (tcgen05_b200.sweep)
+and of the tiles in the kernels' layout; ``launcher`` returns the call that
+evaluates one of them through t5e_mma_dot_batch.  bench.py times these
+launches; ``python -m tcgen05_b200.step`` runs warm-up steps and one step, the
+command the launch-list profiles are taken with.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+
+CASES_PER_PATH = 1_000_000
+MATRIX_TILES = 4096
+TILE_M, TILE_N, TILE_K = 128, 256, 16
+
+
+def kernel_of(spec) -> str:
+    """The specialised kernel t5e_mma_dot_batch dispatches a path to."""
+    d = spec.descriptor
+    fam, fmt = spec.family, d["a_format"]
+    if fam == "i8":
+        return "i8_kernel"
+    if d["scaling"] == "ue4m3":
+        return "nvfp4_kernel"
+    if fam in ("fp4block", "sparse-fp4block"):
+        return "mxf4_kernel"
+    if fmt in ("tf32", "bf16", "f16") or (fam == "sparse" and spec.params[0] in ("tf32", "bf16", "f16")):
+        return "wide_kernel"
+    if fam in ("mx", "sparse-mx") and fmt in ("e2m3", "e3m2", "e2m1"):
+        return "mx_kernel"
+    return "raw_window_kernel"
+
+
+class Launch:
+    """One launch of the step: a path's shard or the matrix tiles' shard,
+    resident in HBM with its output buffer and the batch struct that
+    t5e_mma_dot_batch takes."""
+
+    def __init__(self, name, kernel, desc, db, d, macs, nbytes, first_case):
+        from . import runtime
+
+        self.name, self.kernel, self.desc = name, kernel, desc
+        self.db, self.d = db, d
+        self.struct = runtime.make_batch_struct(db, d, None)
+        self.macs, self.bytes = macs, nbytes
+        self.first_case = first_case  # global index of this shard's first case
+
+
+def build_step(torch, dev, rank: int, world: int, *, cases_per_path: int = CASES_PER_PATH,
+               tiles: int = MATRIX_TILES) -> list[Launch]:
+    """This rank's shard of every path and of the matrix tiles, generated in
+    HBM in the kernels' layout (smaller steps for profiling keep the same
+    distributions)."""
+    from . import sweep, workloads
+
+    items = []
+    lo, hi = sweep.shard(cases_per_path, rank, world)
+    for spec in workloads.validation_paths():
+        model, db = sweep.device_batch(spec, lo, hi - lo, cases_per_path, dev)
+        macs, nbytes = sweep.path_work(spec, db.n, model)
+        d = torch.empty(db.n, dtype=torch.int32, device=dev)
+        items.append(Launch(spec.name, kernel_of(spec), model.descriptor(), db, d, macs, nbytes, lo))
+    t0, t1 = sweep.shard(tiles, rank, world)
+    per_tile = TILE_M * TILE_N
+    model, db = sweep.matrix_tiles(t0, t1 - t0, dev, TILE_M, TILE_N, TILE_K)
+    macs, nbytes = workloads.config_work("matrix-bf16", db)
+    d = torch.empty(db.n, dtype=torch.int32, device=dev)
+    items.append(Launch("matrix-bf16", "wide_tile_kernel", model.descriptor(), db, d, macs, nbytes, t0 * per_tile))
+    torch.cuda.synchronize(dev)
+    return items
+
+
+def launcher(lib, stream):
+    from . import _native as nat
+
+    handle = ctypes.c_void_p(stream.cuda_stream)
+
+    def launch(item):
+        rc = lib.t5e_mma_dot_batch(ctypes.byref(item.desc), ctypes.byref(item.struct), handle)
+        if rc != 0:
+            nat.check(rc, "t5e_mma_dot_batch " + item.name)
+
+    return launch
+
+
+def whole_step_macs() -> int:
+    """Element-MACs of one step of the whole job: physical products of the
+    46 paths at CASES_PER_PATH cases each, plus the matrix tiles."""
+    from . import sweep, workloads
+
+    macs = sum(sweep.path_work(s, CASES_PER_PATH)[0] for s in workloads.validation_paths())
+    return macs + MATRIX_TILES * TILE_M * TILE_N * TILE_K
+
+
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--cases-per-path", type=int, default=CASES_PER_PATH)
+    ap.add_argument("--tiles", type=int, default=MATRIX_TILES)
+    args = ap.parse_args(argv)
+    import torch
+
+    from . import _native as nat
+
+    dev = torch.device("cuda", 0)
+    items = build_step(torch, dev, 0, 1, cases_per_path=args.cases_per_path, tiles=args.tiles)
+    launch = launcher(nat.load(), torch.cuda.current_stream(dev))
+    for _ in range(args.warmup + 1):
+        for item in items:
+            launch(item)
+    torch.cuda.synchronize(dev)
+    print(f"{len(items)} launches per step, {args.warmup} warm-up steps and one step", flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

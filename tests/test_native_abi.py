@@ -110,7 +110,7 @@ def test_empty_batch_is_a_no_op():
 def test_issue_probe_rejects_bad_arguments_without_a_device():
     lib = nat.load()
     count = ctypes.c_uint64(0)
-    assert lib.t5e_issue_probe(2, 1, ctypes.byref(count), None) == nat.ERR_INVALID
+    assert lib.t5e_issue_probe(3, 1, ctypes.byref(count), None) == nat.ERR_INVALID
     assert lib.t5e_issue_probe(-1, 1, ctypes.byref(count), None) == nat.ERR_INVALID
     assert lib.t5e_issue_probe(0, 0, ctypes.byref(count), None) == nat.ERR_INVALID
     assert lib.t5e_issue_probe(0, (1 << 20) + 1, ctypes.byref(count), None) == nat.ERR_INVALID
@@ -121,12 +121,12 @@ def test_issue_probe_rejects_bad_arguments_without_a_device():
 @pytest.mark.gpu
 def test_issue_probe_counts_its_instructions():
     """Two blocks of 1024 threads per SM, 256 probe instructions per thread
-    and iteration, for either pipe."""
+    and iteration, for each pipe (ALU, FMA, FP64)."""
     import torch
 
     lib = nat.load()
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    for pipe in (0, 1):
+    for pipe in (0, 1, 2):
         count = ctypes.c_uint64(0)
         assert lib.t5e_issue_probe(pipe, 4, ctypes.byref(count), None) == nat.OK
         torch.cuda.synchronize()
