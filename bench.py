@@ -567,6 +567,32 @@ def run_ours(args) -> int:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
+    # the step's launches, captured once in a CUDA graph: each timed step is
+    # one graph launch, so the host's launch rate never paces the GPU (the
+    # launches keep their programmatic dependencies inside the graph)
+    graph, graph_note = None, "eager launches (graph capture unavailable)"
+    try:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, capture_error_mode="thread_local"):
+            launch_c = launcher(lib, torch.cuda.current_stream(dev))
+            for item in items:
+                launch_c(item)
+        g.replay()
+        torch.cuda.synchronize(dev)
+        graph, graph_note = g, "one CUDA graph of the step's launches per step"
+    except RuntimeError as exc:  # capture refused: time the launches eagerly
+        print(f"bench: graph capture failed ({exc}); timing eager launches", file=sys.stderr)
+        torch.cuda.synchronize(dev)
+
+    def timed_step():
+        if graph is not None:
+            graph.replay()
+        else:
+            step()
+
+    for _ in range(2):
+        timed_step()
+    torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     sampler = ClockSampler(smi_gpu_id(local))
     sampler.start()
@@ -576,7 +602,7 @@ def run_ours(args) -> int:
     torch.cuda.synchronize(dev)
     e0.record(stream)
     for _ in range(args.steps):
-        step()
+        timed_step()
     e1.record(stream)
     torch.cuda.synchronize(dev)
     if world > 1:
@@ -627,6 +653,7 @@ def run_ours(args) -> int:
     if rank == 0:
         line = report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mismatches + e2e_bad, sums,
                            nv, clocks, e2e_value, e2e_runs, e2e_s, ceiling_s, h2d, d2h, torch, lib, stream)
+        line["timed_launches"] = graph_note
         if world == 1 and not args.no_cpu_baseline:
             line.update(cpu_baselines(items, host, args.cpu_seconds))
         print(json.dumps(line), flush=True)

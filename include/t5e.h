@@ -166,10 +166,11 @@ const char* t5e_last_error(void);
 
 /* Evaluate every case of the batch on the current device, asynchronously on
  * `stream` (a cudaStream_t; NULL = legacy default stream).  Replaces the
- * per-case loop of mma_dot / ScalarModel.eval / mma.  The f8/f6/f4 kernel is
- * launched as a programmatic dependent of the previous kernel on `stream`:
- * its blocks may start early but wait for that kernel to complete before
- * reading any operand, so stream order holds as for any launch. */
+ * per-case loop of mma_dot / ScalarModel.eval / mma.  The specialised
+ * kernels are launched as programmatic dependents of the previous kernel on
+ * `stream`: their blocks may start early but wait for that kernel to complete
+ * before reading any operand, so stream order holds as for any launch, in a
+ * CUDA graph captured from `stream` as well. */
 int t5e_mma_dot_batch(const t5e_model* model, const t5e_batch* batch, void* stream);
 
 /* Same arithmetic through the generic (descriptor-interpreting) kernel only;

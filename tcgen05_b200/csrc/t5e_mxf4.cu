@@ -182,6 +182,9 @@ __device__ __forceinline__ void eval_case(const t5e_batch& B, uint32_t i, const 
 
 template <bool SPARSE, bool A_LOGICAL, int SBLK, int NSCALE>
 __global__ void __launch_bounds__(kThreads) mxf4_kernel(const t5e_batch B) {
+  // programmatic dependent launch, as for the NVFP4 kernel
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t n = (uint32_t)B.n;
   const uint32_t stride = gridDim.x * blockDim.x;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -212,7 +215,11 @@ int launch(const t5e_batch& B, cudaStream_t stream) {
   const uint64_t need = (B.n + kThreads - 1) / kThreads;
   const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
   const int grid = (int)(need < cap ? (need ? need : 1) : cap);
-  kern<<<grid, kThreads, 0, stream>>>(B);
+  const cudaError_t e = launch_dependent(kern, (unsigned)grid, kThreads, 0, stream, B);
+  if (e != cudaSuccess) {
+    set_cuda_error("mxf4_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("mxf4_kernel launch");
 }
 

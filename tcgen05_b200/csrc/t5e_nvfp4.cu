@@ -217,6 +217,11 @@ __device__ __forceinline__ void eval_case(const t5e_batch& B, uint32_t i, const 
 // then cost occupancy.)
 template <bool SPARSE, bool A_LOGICAL>
 __global__ void __launch_bounds__(kThreads) nvfp4_kernel(const t5e_batch B) {
+  // launched as a programmatic dependent of the previous kernel on the
+  // stream: let the next launch place its blocks early, and wait for the
+  // previous grid to complete before any operand is read
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const uint32_t n = (uint32_t)B.n;
   const uint32_t stride = gridDim.x * blockDim.x;
   for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -247,7 +252,11 @@ int launch(const t5e_batch& B, cudaStream_t stream) {
   const uint64_t need = (B.n + kThreads - 1) / kThreads;
   const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
   const int grid = (int)(need < cap ? (need ? need : 1) : cap);
-  nvfp4_kernel<SPARSE, A_LOGICAL><<<grid, kThreads, 0, stream>>>(B);
+  const cudaError_t e = launch_dependent(nvfp4_kernel<SPARSE, A_LOGICAL>, (unsigned)grid, kThreads, 0, stream, B);
+  if (e != cudaSuccess) {
+    set_cuda_error("nvfp4_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("nvfp4_kernel launch");
 }
 

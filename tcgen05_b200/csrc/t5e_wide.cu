@@ -387,9 +387,14 @@ __device__ __forceinline__ void tile_cases(const double* __restrict__ afa, const
 }
 
 template <int F, bool F16D, int R, int BLOCKS>
-__global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_batch B, int floor_raw) {
+__global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_batch B, int floor_raw, int split) {
   using T = Fmt<F>;
   constexpr int K = T::K;
+  // programmatic dependent launch: the next launch may place its blocks as
+  // this grid's last tiles finish; this grid waits for the previous one
+  // before reading any tile
+  asm volatile("griddepcontrol.launch_dependents;");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   extern __shared__ int4 smem4[];
   const int tm = B.tile_m, tn = B.tile_n;
   double* afa = reinterpret_cast<double*>(smem4);                    // [tm][K] element values
@@ -400,15 +405,21 @@ __global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_b
   const uint8_t* Bbase = static_cast<const uint8_t*>(B.b);
   const uint32_t tiles = (uint32_t)(B.n / ((uint64_t)tm * (uint64_t)tn));
   constexpr int kCBytes = F16D ? 2 : 4;
-  for (uint32_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    __syncthreads();  // the previous tile's rows are no longer read
-    for (int row = threadIdx.x; row < tm; row += blockDim.x) aspecial[row] = 0;
+  // a unit of work is a block of `rows` rows of one tile: whole tiles when
+  // there are enough of them to spread evenly over the resident blocks
+  const int rows = tm / split;
+  const uint32_t units = tiles * (uint32_t)split;
+  for (uint32_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const uint32_t t = u / (uint32_t)split;
+    const int r0 = (int)(u - t * (uint32_t)split) * rows;
+    __syncthreads();  // the previous unit's rows are no longer read
+    for (int row = threadIdx.x; row < rows; row += blockDim.x) aspecial[row] = 0;
     __syncthreads();
-    // the tile's A rows, two elements per step
-    for (int e2 = threadIdx.x; e2 < tm * (K / 2); e2 += blockDim.x) {
+    // the unit's A rows, two elements per step
+    for (int e2 = threadIdx.x; e2 < rows * (K / 2); e2 += blockDim.x) {
       const int row = e2 / (K / 2), k = 2 * (e2 - row * (K / 2));
       uint32_t wa[8];
-      load32(Abase + ((size_t)t * tm + row) * 32, wa);
+      load32(Abase + ((size_t)t * tm + r0 + row) * 32, wa);
       double v0, v1;
       uint32_t r0, r1;
       bool n0, i0, n1, i1;
@@ -437,10 +448,10 @@ __global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_b
         binf |= i0 | i1;
       }
       bflag[j] = (bnan ? 1 : 0) | (binf ? 2 : 0);
-      // this column's cases, one row of the tile apart
-      const size_t case0 = (size_t)t * tm * tn + j;
+      // this column's cases in the unit, one row of the tile apart
+      const size_t case0 = ((size_t)t * tm + r0) * tn + j;
       if (B.status)
-        for (int i = 0; i < tm; ++i) B.status[case0 + (size_t)i * tn] = (uint8_t)T5E_CASE_OK;
+        for (int i = 0; i < rows; ++i) B.status[case0 + (size_t)i * tn] = (uint8_t)T5E_CASE_OK;
       const uint8_t* ccol = static_cast<const uint8_t*>(B.c) + case0 * kCBytes;
       const size_t cstep = (size_t)tn * kCBytes;
       auto c_load = [](const uint8_t* p) {
@@ -450,12 +461,12 @@ __global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_b
       uint32_t c_next[R];  // the next rows' C words are in flight while these rows are evaluated
 #pragma unroll
       for (int r = 0; r < R; ++r) c_next[r] = c_load(ccol + (size_t)r * cstep);
-      for (int i = 0; i < tm; i += R) {
+      for (int i = 0; i < rows; i += R) {
         uint32_t cword[R], out[R];
 #pragma unroll
         for (int r = 0; r < R; ++r) {
           cword[r] = c_next[r];
-          if (i + R + r < tm) c_next[r] = c_load(ccol + (size_t)(i + R + r) * cstep);
+          if (i + R + r < rows) c_next[r] = c_load(ccol + (size_t)(i + R + r) * cstep);
         }
         tile_cases<F, F16D, R>(afa, ar2, i, fb, br2, cword, floor_raw, out);
 #pragma unroll
@@ -476,8 +487,8 @@ __global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_b
       if (bf & 1) continue;
       uint32_t wb[8];
       bool loaded = false;
-      const size_t case0 = (size_t)t * tm * tn + j;
-      for (int i = 0; i < tm; ++i) {
+      const size_t case0 = ((size_t)t * tm + r0) * tn + j;
+      for (int i = 0; i < rows; ++i) {
         const int af = aspecial[i];
         if ((af & 1) || !(bf | af)) continue;
         if (!loaded) {
@@ -488,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, BLOCKS) wide_tile_kernel(const t5e_b
         const uint32_t cword = F16D ? (uint32_t)__ldg(static_cast<const uint16_t*>(B.c) + ci)
                                     : __ldg(static_cast<const uint32_t*>(B.c) + ci);
         uint32_t wa[8];
-        load32(Abase + ((size_t)t * tm + i) * 32, wa);
+        load32(Abase + ((size_t)t * tm + r0 + i) * 32, wa);
         B.d[ci] = eval_rows<F, F16D>(wa, wb, cword, floor_raw);
         if (B.status) B.status[ci] = (uint8_t)T5E_CASE_OK;
       }
@@ -542,8 +553,20 @@ int launch_tiles(const t5e_batch& B, int floor_raw, cudaStream_t stream) {
     per_sm = 1;
   const uint64_t tiles = B.n / ((uint64_t)B.tile_m * (uint64_t)B.tile_n);
   const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
-  const int grid = (int)(tiles < cap ? (tiles ? tiles : 1) : cap);
-  wide_tile_kernel<F, F16D, R, BLOCKS><<<grid, threads, smem, stream>>>(B, floor_raw);
+  // split tiles into row blocks (of at least 16 rows, whole R-row steps)
+  // until there are about eight units per resident block, so that the last
+  // round of units leaves few blocks idle
+  int split = 1;
+  while (tiles * (uint64_t)split < 8 * cap && B.tile_m % (2 * split * R) == 0 && B.tile_m / (2 * split) >= 16)
+    split *= 2;
+  const uint64_t units = tiles * (uint64_t)split;
+  const int grid = (int)(units < cap ? (units ? units : 1) : cap);
+  const cudaError_t e = launch_dependent(wide_tile_kernel<F, F16D, R, BLOCKS>, (unsigned)grid, (unsigned)threads,
+                                         (size_t)smem, stream, B, floor_raw, split);
+  if (e != cudaSuccess) {
+    set_cuda_error("wide_tile_kernel launch", e);
+    return T5E_ERR_CUDA;
+  }
   return kernel_status("wide_tile_kernel launch");
 }
 

@@ -772,3 +772,34 @@ def test_f16_d_rounding_edges(a_format, b_format):
     got = gpu_cases(cases)
     assert_words_equal(got, oracle.eval_cases(cases), f"{a_format}x{b_format} F16 D edges vs oracle")
     assert_words_equal(got, gpu_cases(cases, generic=True), f"{a_format}x{b_format} F16 D edges vs generic")
+
+
+def test_step_launches_replay_from_a_cuda_graph():
+    """The step's launches (every path's kernel and the matrix tiles, with
+    their programmatic dependencies) captured in a CUDA graph give the words
+    of the same launches made eagerly."""
+    import torch
+
+    from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import step
+
+    dev = torch.device("cuda", 0)
+    items = step.build_step(torch, dev, 0, 1, cases_per_path=1 << 16, tiles=8)
+    lib = nat.load()
+    eager = step.launcher(lib, torch.cuda.current_stream(dev))
+    for item in items:
+        eager(item)
+    torch.cuda.synchronize(dev)
+    want = [item.d.clone() for item in items]
+    for item in items:
+        item.d.fill_(-1)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, capture_error_mode="thread_local"):
+        captured = step.launcher(lib, torch.cuda.current_stream(dev))
+        for item in items:
+            captured(item)
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    for item, w in zip(items, want):
+        assert torch.equal(item.d, w), item.name
