@@ -67,22 +67,25 @@ __global__ void __launch_bounds__(kThreads, kBlocksPerSm) issue_kernel(uint32_t 
   if (acc == 0x2545F491u && seed == 0x68E31DA4u) g_sink[blockIdx.x & 1023u] = acc;
 }
 
-// FP64 pipe: DFMA chains, the pipe the matrix tile kernel forms and
-// truncates its terms on.  Values stay near 1 (x*p + q with p, q in
-// [0.25, 0.75)), so no chain reaches a special value.
+// FP64 pipe: DFMA chains (x[c] * x[c+1] + x[c+3], one instruction per
+// chain and step), the pipe the matrix tile kernel forms and truncates its
+// terms on.  The values start near 2**-10 and each step adds about 2**-20,
+// so over the 256 iterations (8192 steps) bench.py runs they stay near
+// 2**-10, far from any special value.
 __global__ void __launch_bounds__(kThreads, kBlocksPerSm) issue_kernel_fp64(uint32_t iters, uint32_t seed) {
   double x[kChains];
 #pragma unroll
   for (int c = 0; c < kChains; ++c)
-    x[c] = 0.25 + 0.5 * (double)(((seed + 0x9E3779B9u * (uint32_t)(c + 1)) ^ threadIdx.x) & 0xFFFFu) / 65536.0;
+    x[c] = (1.0 + (double)(((seed + 0x9E3779B9u * (uint32_t)(c + 1)) ^ threadIdx.x) & 0xFFFFu) / 65536.0) / 1024.0;
   for (uint32_t it = 0; it < iters; ++it) {
 #pragma unroll
     for (int s = 0; s < kSteps; ++s) {
       double y[kChains];
 #pragma unroll
       for (int c = 0; c < kChains; ++c) {
-        const double p = 0.25 + 0.5 * x[(c + 1) % kChains], q = 0.25 * x[(c + 3) % kChains];
-        asm volatile("fma.rn.f64 %0, %1, %2, %3;" : "=d"(y[c]) : "d"(x[c]), "d"(p), "d"(q));
+        asm volatile("fma.rn.f64 %0, %1, %2, %3;"
+                     : "=d"(y[c])
+                     : "d"(x[c]), "d"(x[(c + 1) % kChains]), "d"(x[(c + 3) % kChains]));
       }
 #pragma unroll
       for (int c = 0; c < kChains; ++c) x[c] = y[c];
