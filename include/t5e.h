@@ -286,6 +286,37 @@ int t5e_tcgen05_block_scaled_tiles(int32_t kind, uint32_t idesc, const void* a, 
                                    uint32_t* d, const uint32_t* scale_a, const uint32_t* scale_b, uint64_t tiles,
                                    int32_t* error, void* stream);
 
+/* The sparse kinds (tcgen05.mma.sp; no counterpart in the reference's model
+ * package: the role of its harness's sparse probe runners,
+ * hardware_validation/src/tcgen05_*_sparse_probe.cu).  One uniform tile per
+ * case: M = 64 (kind::tf32, kind::f16, kind::f8f6f4) or M = 128 (the
+ * block-scaled kinds), N = 8, every row of A the case's compressed A row,
+ * every column of B its logical-K row, every element of C its c word, every
+ * row's metadata (and scale word) the case's; all elements of D are then one
+ * scalar.
+ *   a: cases*32 bytes (half the logical K, in the order the metadata selects),
+ *   b: cases*64 bytes (the logical K), both 16-byte aligned, in the operand
+ *   forms of the dense tiles above; c: cases words (F32);
+ *   meta: cases*2 words (selectors of K chunks 0-7, then 8-15);
+ *   scales: cases*2 words for the block-scaled kinds (A's, then B's; byte j
+ *   = scale block j), NULL otherwise;
+ *   d: cases words, D[0][0] of each tile; disagree: cases words, the number
+ *   of the tile's other D elements that differ from it; dump: NULL, or
+ *   cases*1024 words receiving TMEM columns 0-7 of all 128 lanes.
+ * `meta_layout` (0-2) picks the word pattern the metadata region is filled
+ * with (0: the two words in alternate columns; 1: lanes 0-7 of each 16 the
+ * low half of the first word in both halves, lanes 8-15 its high half;
+ * 2: lanes 0-7 of each 16 the first word, 8-15 the second).  `idesc` must
+ * set the sparse flag, N = 8 and the kind's M; other encodings are rejected
+ * before any launch.  *error as for t5e_tcgen05_tiles. */
+enum {
+  T5E_HW_SP_TF32 = 8, T5E_HW_SP_F16 = 9, T5E_HW_SP_F8F6F4 = 10, T5E_HW_SP_MXF8F6F4 = 11, T5E_HW_SP_MXF4 = 12,
+  T5E_HW_SP_MXF4NVF4_2X = 13, T5E_HW_SP_MXF4NVF4_4X = 14
+};
+int t5e_tcgen05_sparse_cases(int32_t kind, uint32_t idesc, int32_t meta_layout, const void* a, const void* b,
+                             const uint32_t* c, const uint32_t* meta, const uint32_t* scales, uint32_t* d,
+                             int32_t* disagree, uint32_t* dump, uint64_t cases, int32_t* error, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

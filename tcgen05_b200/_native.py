@@ -120,6 +120,7 @@ EXPORTED = (
     "t5e_sparse_active",
     "t5e_tcgen05_tiles",
     "t5e_tcgen05_block_scaled_tiles",
+    "t5e_tcgen05_sparse_cases",
 )
 
 _lib = None
@@ -173,6 +174,9 @@ def load() -> ctypes.CDLL:
                                                    ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                                    ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p,
                                                    ctypes.c_void_p]
+    lib.t5e_tcgen05_sparse_cases.restype = ctypes.c_int
+    lib.t5e_tcgen05_sparse_cases.argtypes = [ctypes.c_int32, ctypes.c_uint32, ctypes.c_int32] + [ctypes.c_void_p] * 8 \
+        + [ctypes.c_uint64, ctypes.c_void_p, ctypes.c_void_p]
     version = lib.t5e_abi_version()
     if version != ABI_VERSION:
         raise NativeLibraryError(f"{LIB_PATH} has ABI version {version}, expected {ABI_VERSION}; rebuild it")

@@ -12,6 +12,10 @@ library.  Every word agrees, except that on the F16 x F16 -> F16 path the
 reference (and so the emulator) reports NaN and infinities with F32 words
 where the B200 writes F16 words; that pairing is counted separately.
 
+``cross_check_block_scaled`` does the same for the block-scaled kinds, and
+``cross_check_sparse`` for the sparse ones (tcgen05.mma.sp): the cases of a
+sparse validation path, one uniform tile per case.
+
     python -m tcgen05_b200.hwcheck [--tiles 64] [--seed 0]
 """
 
@@ -377,10 +381,178 @@ BS_PAIRS = tuple(("mxf8f6f4", fa, fb, "ue8m0") for fa, fb in itertools.product(F
     ("mxf4nvf4-4x", "e2m1", "e2m1", "ue8m0"), ("mxf4nvf4-4x", "e2m1", "e2m1", "ue4m3"))
 
 
+# ---- sparse kinds ------------------------------------------------------
+#
+# tcgen05.mma.sp on uniform tiles, one case per tile (t5e_tcgen05_sparse_cases):
+# the sparse validation paths' own cases (sweep.host_cases), A compressed in
+# the order its metadata selects (a 2:4 selector's low index first, as the
+# reference harness packs it, hardware_validation/src/
+# tcgen05_block_scaled_sparse_probe.cu:304-321), B at the logical K.  The
+# emulator side is mma_dot_batch on the same logical cases with their
+# metadata.
+SP_KINDS = {"tf32": 8, "f16": 9, "f8f6f4": 10, "mxf8f6f4": 11, "mxf4": 12, "mxf4nvf4-2x": 13, "mxf4nvf4-4x": 14}
+SP_N = 8
+SP_SCALED = ("mxf8f6f4", "mxf4", "mxf4nvf4-2x", "mxf4nvf4-4x")
+SP_PACKED_E2M1 = ("mxf4", "mxf4nvf4-2x", "mxf4nvf4-4x")
+# metadata word pattern per kind (t5e_tcgen05_sparse_cases' meta_layout): the
+# reference harness's patterns, 16-bit halves by lane for kind::tf32 and
+# kind::f16, the two words in alternate columns otherwise
+SP_LAYOUT = {"tf32": 1, "f16": 1}
+
+
+def sparse_kind(spec) -> tuple[str, str | None]:
+    """(sparse instruction kind, scale format or None) of a sparse validation path."""
+    fam, fmt = spec.family, spec.descriptor["a_format"]
+    if fam == "sparse":
+        return ("tf32" if fmt == "tf32" else "f16" if fmt in ("bf16", "f16") else "f8f6f4"), None
+    if fam == "sparse-mx":
+        return "mxf8f6f4", "ue8m0"
+    if fam == "sparse-nvfp4":
+        return "mxf4nvf4-4x", "ue4m3"
+    if fam == "sparse-fp4block":
+        kind = spec.params[0]
+        return ("mxf4nvf4-4x" if kind.startswith("mxf4nvf4-4x") else kind), \
+            ("ue4m3" if kind.endswith("ue4m3") else "ue8m0")
+    raise ValueError(f"{spec.name} is not a sparse path")
+
+
+def sparse_desc(kind: str, a_format: str, scale: str | None = None) -> int:
+    """Sparse instruction descriptor of a uniform tile: the sparse flag (bit
+    2), formats, N = 8, M = 64 (M = 128 for the block-scaled kinds), an F32
+    accumulator or the scale format."""
+    if kind not in SP_KINDS:
+        raise ValueError(f"unknown sparse kind {kind}")
+    scaled = kind in SP_SCALED
+    fa = MXF4_E2M1 if kind in SP_PACKED_E2M1 else FORMAT_CODES[a_format]
+    desc = (1 << 2) | (fa << 7) | (fa << 10) | ((SP_N >> 3) << 17) | (((128 if scaled else 64) >> 4) << 24)
+    if scaled:
+        return desc | ((1 if scale == "ue8m0" else 0) << 23)
+    return desc | (C_FORMATS["f32"] << 4)
+
+
+def operand_bytes(words, fmt: str, kind: str) -> np.ndarray:
+    """[R, K] words -> [R, bytes] operand rows: packed E2M1 for the mxf4
+    kinds, 16-byte chunks of 16 packed elements (zero padded) for
+    E2M3/E3M2/E2M1 in the f8f6f4 kinds, packed little-endian otherwise."""
+    w = np.asarray(words, dtype=np.uint32)
+    rows, k = w.shape
+    if kind in SP_PACKED_E2M1:
+        return packing.pack_rows(w, nat.FORMAT_IDS["e2m1"])
+    fid = nat.FORMAT_IDS[fmt]
+    if fmt in SUB_BYTE:
+        if k % 16:
+            raise ValueError("f8f6f4 sub-byte rows hold whole 16-element chunks")
+        return packing.pack_rows(w.reshape(rows * (k // 16), 16), fid, stride=16).reshape(rows, k)
+    return packing.pack_rows(w, fid)
+
+
+def compress_a(a, meta, k: int, mode: str) -> np.ndarray:
+    """Logical A rows [n, k] -> the k/2 elements each row's metadata selects,
+    in selector order: 1:2 takes element 1 of a pair for selector 0xE and
+    element 0 otherwise; 2:4 the two 2-bit indices of a nibble, low first;
+    pairwise 4:8 the two pairs a nibble names, low first."""
+    a = np.asarray(a, dtype=np.uint32)
+    meta = np.asarray(meta, dtype=np.uint32)
+    n = a.shape[0]
+    rows = np.arange(n)
+    size = {"1of2": 2, "2of4": 4, "4of8": 8}[mode]
+    out = np.zeros((n, k // 2), dtype=np.uint32)
+    for ch in range(k // size):
+        sel = (meta[:, 0 if ch < 8 else 1] >> np.uint32(4 * (ch % 8))) & 0xF
+        if mode == "1of2":
+            out[:, ch] = a[rows, 2 * ch + (sel == 0xE)]
+        elif mode == "2of4":
+            for j in range(2):
+                out[:, 2 * ch + j] = a[rows, 4 * ch + ((sel >> np.uint32(2 * j)) & 3)]
+        else:
+            for j in range(4):
+                pair = (sel >> np.uint32(2 * (j // 2))) & 3
+                out[:, 4 * ch + j] = a[rows, 8 * ch + 2 * pair + (j & 1)]
+    return out
+
+
+def hardware_sparse_cases(cases, spec, *, layout: int | None = None, dump: bool = False, device=None) -> dict:
+    """Run a sparse path's cases (a ``workloads.Cases`` of logical words and
+    metadata) as uniform tcgen05.mma.sp tiles: {"d": words, "disagree":
+    per-case counts, "dump": [n, 128, 8] TMEM words or None}."""
+    _refuse_after_timeout()
+    import torch
+
+    from . import sweep
+
+    kind, scale = sparse_kind(spec)
+    fmt = spec.descriptor["a_format"]
+    desc = sparse_desc(kind, fmt, scale)
+    layout = SP_LAYOUT.get(kind, 0) if layout is None else layout
+    mode = sweep.sparse_mode(spec)
+    n, k = cases.a.shape
+    a_rows = operand_bytes(compress_a(cases.a, cases.meta, k, mode), fmt, kind)
+    b_rows = operand_bytes(cases.b, fmt, kind)
+    if a_rows.shape[1] != 32 or b_rows.shape[1] != 64:
+        raise ValueError(f"{spec.name}: operand rows of {a_rows.shape[1]} / {b_rows.shape[1]} bytes, expected 32 / 64")
+    meta = np.zeros((n, 2), dtype=np.uint32)
+    meta[:, : cases.meta.shape[1]] = cases.meta
+    if cases.meta.shape[1] == 1:
+        meta[:, 1] = cases.meta[:, 0]
+    dev = runtime.require_device(device)
+    scales_dev = None
+    if kind in SP_SCALED:
+        blocks = sweep.scale_blocks(spec)
+        sw = np.stack([scale_words(cases.scale_a[:, :blocks]), scale_words(cases.scale_b[:, :blocks])], axis=1)
+        scales_dev = runtime.to_device(np.ascontiguousarray(sw).reshape(-1), dev)
+    a_dev = runtime.to_device(np.ascontiguousarray(a_rows), dev)
+    b_dev = runtime.to_device(np.ascontiguousarray(b_rows), dev)
+    c_dev = runtime.to_device(np.asarray(cases.c, dtype=np.uint32), dev)
+    m_dev = runtime.to_device(meta.reshape(-1), dev)
+    d_dev = torch.zeros(n, dtype=torch.int32, device=dev)
+    bad_dev = torch.zeros(n, dtype=torch.int32, device=dev)
+    dump_dev = torch.zeros(n * 128 * SP_N, dtype=torch.int32, device=dev) if dump else None
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    lib = nat.load()
+    stream = ctypes.c_void_p(runtime.current_stream_handle(dev))
+    ptr = lambda x: None if x is None else x.data_ptr()  # noqa: E731
+    rc = lib.t5e_tcgen05_sparse_cases(SP_KINDS[kind], desc, layout, a_dev.data_ptr(), b_dev.data_ptr(),
+                                      c_dev.data_ptr(), m_dev.data_ptr(), ptr(scales_dev), d_dev.data_ptr(),
+                                      bad_dev.data_ptr(), ptr(dump_dev), n, err.data_ptr(), stream)
+    nat.check(rc, "t5e_tcgen05_sparse_cases")
+    torch.cuda.synchronize(dev)
+    _check_wait(err)
+    out = {"d": d_dev.cpu().numpy().view(np.uint32), "disagree": bad_dev.cpu().numpy(), "dump": None}
+    if dump:
+        out["dump"] = dump_dev.cpu().numpy().view(np.uint32).reshape(n, 128, SP_N)
+    return out
+
+
+def cross_check_sparse(spec, n: int = 1024, *, layout: int | None = None, device=None) -> dict:
+    """Hardware and emulator words of the first n cases of a sparse path."""
+    from . import sweep
+    from .simulator import mma_dot_batch
+
+    cases = sweep.host_cases(spec, 0, n, n)
+    hw = hardware_sparse_cases(cases, spec, layout=layout, device=device)
+    d = spec.descriptor
+    kw = {key: d[key] for key in ("a_format", "b_format", "d_type", "saturate", "scaling", "scale_vec", "kind")}
+    emu = np.asarray(mma_dot_batch(cases.a, cases.b, cases.c, scale_a=cases.scale_a, scale_b=cases.scale_b,
+                                   sparse_metadata=cases.meta, device=device, **kw), dtype=np.uint32)
+    diff = np.flatnonzero(hw["d"] != emu)
+    kind, scale = sparse_kind(spec)
+    return {"path": spec.name, "kind": kind, "scale": scale, "layout": SP_LAYOUT.get(kind, 0) if layout is None
+            else layout, "cases": n, "mismatches": int(diff.size), "first": [int(i) for i in diff[:8]],
+            "nonuniform_tiles": int((hw["disagree"] != 0).sum()), "hardware": hw["d"], "emulator": emu}
+
+
+def sparse_paths():
+    """The sparse validation paths, in workload order."""
+    from . import workloads
+
+    return [p for p in workloads.validation_paths() if p.family.startswith("sparse")]
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--tiles", type=int, default=64)
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--sparse-cases", type=int, default=1024)
     args = ap.parse_args(argv)
     failed = 0
     for i, (fa, fb, sat, d) in enumerate(PAIRS):
@@ -395,9 +567,15 @@ def main(argv=None) -> int:
         r = cross_check_block_scaled(a, b, c, sa, sb, kind, fa, fb, scale)
         bs_failed += r["mismatches"] != 0
         print(json.dumps({k: v for k, v in r.items() if k not in ("hardware", "emulator")}), flush=True)
+    sp_failed = 0
+    for spec in sparse_paths():
+        r = cross_check_sparse(spec, args.sparse_cases)
+        sp_failed += r["mismatches"] != 0 or r["nonuniform_tiles"] != 0
+        print(json.dumps({k: v for k, v in r.items() if k not in ("hardware", "emulator")}), flush=True)
     print(json.dumps({"pairs": len(PAIRS), "pairs_with_mismatches": failed, "block_scaled_pairs": len(BS_PAIRS),
-                      "block_scaled_pairs_with_mismatches": bs_failed}), flush=True)
-    return 1 if failed or bs_failed else 0
+                      "block_scaled_pairs_with_mismatches": bs_failed, "sparse_paths": len(sparse_paths()),
+                      "sparse_paths_with_mismatches": sp_failed}), flush=True)
+    return 1 if failed or bs_failed or sp_failed else 0
 
 
 if __name__ == "__main__":

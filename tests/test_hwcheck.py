@@ -273,3 +273,134 @@ def test_tcgen05_block_scaled_hardware_equals_emulator(kind, fa, fb, scale):
     assert r["mismatches"] == 0, (f"{r['mismatches']} of {r['cases']} words differ; first cases {r['first']}: "
                                   f"hardware {[hex(int(x)) for x in r['hardware'].reshape(-1)[r['first']]]} "
                                   f"emulator {[hex(int(x)) for x in r['emulator'].reshape(-1)[r['first']]]}")
+
+
+# ---- sparse kinds ------------------------------------------------------
+
+# (kind, operand format, scale format, CUTLASS operand type, scale type or None)
+SP_CASES = [("tf32", "tf32", None, "tfloat32_t", None),
+            ("f16", "bf16", None, "bfloat16_t", None),
+            ("f16", "f16", None, "half_t", None),
+            ("f8f6f4", "e4m3", None, "float_e4m3_t", None),
+            ("f8f6f4", "e3m2", None, _E3M2, None),
+            ("f8f6f4", "e2m1", None, _E2M1, None),
+            ("mxf8f6f4", "e5m2", "ue8m0", "float_e5m2_t", "float_ue8m0_t"),
+            ("mxf8f6f4", "e2m3", "ue8m0", _E2M3, "float_ue8m0_t"),
+            ("mxf4", "e2m1", "ue8m0", "float_e2m1_t", "float_ue8m0_t"),
+            ("mxf4nvf4-4x", "e2m1", "ue4m3", "float_e2m1_t", "float_ue4m3_t")]
+
+
+def test_sparse_descriptors_match_cutlass(tmp_path):
+    inc = _cutlass_include()
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if inc is None or not os.path.exists(nvcc):
+        pytest.skip("CUTLASS headers or nvcc not available")
+    lines = ["#include <cstdio>", "#include <cute/arch/mma_sm100_desc.hpp>",
+             "#include <cute/numeric/numeric_types.hpp>", "using namespace cute;", "int main() {"]
+    for kind, _, _, t, tsf in SP_CASES:
+        if tsf is None:
+            lines.append(f'  printf("%u\\n", uint32_t(UMMA::make_instr_desc<{t}, {t}, float, 64, 8, UMMA::Major::K, '
+                         f'UMMA::Major::K, UMMA::ScaleIn::One, UMMA::ScaleIn::One, UMMA::Saturate::False, true>()));')
+        else:
+            lines.append(f'  printf("%u\\n", uint32_t(UMMA::make_instr_desc_block_scaled<{t}, {t}, float, {tsf}, '
+                         f'128, 8, UMMA::Major::K, UMMA::Major::K, UMMA::ScaleIn::One, UMMA::ScaleIn::One, true>()));')
+    lines.append("  return 0; }")
+    src = tmp_path / "sp.cu"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "sp"
+    subprocess.run([nvcc, "-std=c++17", "-I", str(inc), "-o", str(exe), str(src)], check=True,
+                   capture_output=True, timeout=600)
+    want = [int(x) for x in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split()]
+    got = [hwcheck.sparse_desc(kind, fmt, scale) for kind, fmt, scale, *_ in SP_CASES]
+    assert got == want
+
+
+def test_sparse_paths_map_onto_the_sparse_kinds():
+    paths = hwcheck.sparse_paths()
+    assert len(paths) == 18
+    kinds = {p.name: hwcheck.sparse_kind(p) for p in paths}
+    assert kinds["sparse-tf32"] == ("tf32", None)
+    assert kinds["sparse-bf16"] == kinds["sparse-f16"] == ("f16", None)
+    assert kinds["sparse-e2m1"] == ("f8f6f4", None)
+    assert kinds["sparse-mx-e2m1"] == ("mxf8f6f4", "ue8m0")
+    assert kinds["sparse-nvfp4"] == kinds["sparse-mxf4nvf4-4x-ue4m3"] == ("mxf4nvf4-4x", "ue4m3")
+    assert kinds["sparse-mxf4nvf4-4x"] == ("mxf4nvf4-4x", "ue8m0")
+    assert kinds["sparse-mxf4"] == ("mxf4", "ue8m0")
+    with pytest.raises(ValueError):
+        hwcheck.sparse_desc("i8", "s8")
+
+
+def test_sparse_compression_follows_the_selector_order():
+    """Each compressed row holds exactly the elements its metadata selects
+    (every sparse path), in the order of the selector's indices: a 2:4
+    selector 0x6 names index 2 first, so the compressed pair is (a[2], a[1])."""
+    from tcgen05_b200 import sweep
+
+    for spec in hwcheck.sparse_paths():
+        cases = sweep.host_cases(spec, 0, 64, 64)
+        mode = sweep.sparse_mode(spec)
+        k = cases.a.shape[1]
+        comp = hwcheck.compress_a(cases.a, cases.meta, k, mode)
+        act = sweep._active(np, cases.meta.astype(np.int64), k, mode)
+        assert comp.shape == (64, k // 2)
+        assert (np.sort(comp, 1) == np.sort(cases.a[act].reshape(64, -1), 1)).all(), spec.name
+        kind, _ = hwcheck.sparse_kind(spec)
+        rows_a = hwcheck.operand_bytes(comp, spec.descriptor["a_format"], kind)
+        rows_b = hwcheck.operand_bytes(cases.b, spec.descriptor["a_format"], kind)
+        assert rows_a.shape == (64, 32) and rows_b.shape == (64, 64), spec.name
+    a = np.arange(16, dtype=np.uint32).reshape(1, 16) + 100
+    meta = np.array([[0x6666_6666 & 0xFFFF_FFFF, 0]], dtype=np.uint32)
+    assert list(hwcheck.compress_a(a, meta, 16, "2of4")[0, :2]) == [102, 101]
+    assert list(hwcheck.compress_a(a, np.array([[0x4E4E_4E4E, 0]], dtype=np.uint32), 16, "1of2")[0, :2]) == [101, 102]
+    assert list(hwcheck.compress_a(a, np.array([[0x0000_0009, 0]], dtype=np.uint32), 16, "4of8")[0, :4]) == \
+        [102, 103, 104, 105]
+
+
+def test_abi_rejects_sparse_descriptors_outside_the_documented_encodings():
+    lib = nat.load()
+    fake = ctypes.c_void_p(1 << 20)
+    kf = hwcheck.SP_KINDS["f16"]
+    df = hwcheck.sparse_desc("f16", "bf16")
+    km = hwcheck.SP_KINDS["mxf8f6f4"]
+    dm = hwcheck.sparse_desc("mxf8f6f4", "e4m3", "ue8m0")
+    k4 = hwcheck.SP_KINDS["mxf4nvf4-2x"]
+    d4 = hwcheck.sparse_desc("mxf4nvf4-2x", "e2m1", "ue8m0")
+    bad = [
+        (kf, df & ~(1 << 2), 0),                         # dense
+        (kf, df | 1, 0),                                 # sparsity selector 1
+        (kf, (df & ~(0x3F << 17)) | (2 << 17), 0),       # N = 16
+        (kf, (df & ~(0x1F << 24)) | (8 << 24), 0),       # M = 128 on an unscaled kind
+        (kf, df & ~(3 << 4), 0),                         # F16 accumulator
+        (kf, df & ~(1 << 10), 0),                        # F16 B with BF16 A
+        (kf, df | (1 << 15), 0),                         # A MN-major
+        (km, (dm & ~(0x1F << 24)) | (4 << 24), 0),       # M = 64 on a block-scaled kind
+        (km, dm & ~(1 << 23), 0),                        # UE4M3 on mxf8f6f4
+        (k4, d4 & ~(1 << 23), 0),                        # UE4M3 on the two-scale mxf4nvf4
+        (kf, df, 3),                                     # unknown metadata layout
+        (15, df, 0),                                     # unknown kind
+    ]
+    for kind, desc, layout in bad:
+        rc = lib.t5e_tcgen05_sparse_cases(kind, desc, layout, fake, fake, fake, fake, fake, fake, fake, None, 1,
+                                          fake, None)
+        assert rc == nat.ERR_INVALID, (kind, hex(desc), layout, rc)
+    rc = lib.t5e_tcgen05_sparse_cases(km, dm, 0, fake, fake, fake, fake, None, fake, fake, None, 1, fake, None)
+    assert rc == nat.ERR_INVALID  # block-scaled kinds need their scale words
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("spec", hwcheck.sparse_paths(), ids=[p.name for p in hwcheck.sparse_paths()])
+def test_tcgen05_sparse_hardware_equals_emulator(spec):
+    r = hwcheck.cross_check_sparse(spec, 512)
+    assert r["nonuniform_tiles"] == 0, f"{r['nonuniform_tiles']} tiles hold more than one D value"
+    assert r["mismatches"] == 0, (f"{r['mismatches']} of {r['cases']} words differ; first cases {r['first']}: "
+                                  f"hardware {[hex(int(x)) for x in r['hardware'][r['first']]]} "
+                                  f"emulator {[hex(int(x)) for x in r['emulator'][r['first']]]}")
+
+
+@pytest.mark.gpu
+def test_sparse_metadata_pattern_is_what_the_hardware_reads():
+    """The same cases with the kind::f16 metadata pattern on a kind::f8f6f4
+    path give other words: the cross-check sees the metadata it is fed."""
+    spec = next(p for p in hwcheck.sparse_paths() if p.name == "sparse-fp8")
+    r = hwcheck.cross_check_sparse(spec, 128, layout=1)
+    assert r["mismatches"] > 0
