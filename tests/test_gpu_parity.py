@@ -339,6 +339,51 @@ def test_matrix_configuration_tiles_fast_equals_generic(desc, k):
     assert_words_equal(fast.reshape(-1)[idx], want, f"{desc} tiles sample vs oracle")
 
 
+@pytest.mark.parametrize("desc,k", [(dict(a_format="bf16"), 16), (dict(a_format="tf32"), 8),
+                                    (dict(a_format="f16", d_type="f16"), 16)])
+def test_tiles_with_infinities_and_zeros_match_oracle(desc, k):
+    """Tiles whose A rows and B columns hold infinities of either sign and
+    finite zeros but no NaN, with C NaN or infinite in some cases: every
+    combination the tile kernel resolves from its masks (infinity times zero,
+    infinities of both signs, C's infinity joining them) equals the oracle."""
+    d = full_desc(desc)
+    rng = np.random.Generator(np.random.PCG64(4242))
+    t, m, n = 2, 128, 256
+    fmt = t5.normalize_format(d["a_format"])
+    pinf, ninf, pz, nz = {"tf32": (0x7F800000, 0xFF800000, 0, 0x80000000),
+                          "bf16": (0x7F800000, 0xFF800000, 0, 0x80000000),
+                          "f16": (0x7C00, 0xFC00, 0, 0x8000)}[fmt]
+    finite = lambda count: workloads.format_words(fmt, rng, count, True)  # noqa: E731
+
+    def rows(count):
+        w = finite(count * k).reshape(count, k)
+        kind = rng.integers(0, 6, size=count)  # 0-1 finite rows; else one or two planted specials
+        for r in np.flatnonzero(kind >= 2):
+            for pos in rng.choice(k, size=1 + (kind[r] >= 4), replace=False):
+                w[r, pos] = (pinf, ninf, pz, nz)[rng.integers(0, 4)]
+        return w
+
+    a = rows(t * m).reshape(t, m, k)
+    bt = rows(t * n).reshape(t, n, k)
+    b = bt.transpose(0, 2, 1).copy()
+    c = (workloads.f16_words(rng, t * m * n, True) if d["d_type"] == "f16"
+         else workloads.f32_words(rng, t * m * n, True))
+    cspecial = np.array(([0x7C00, 0xFC00, 0x7E00] if d["d_type"] == "f16" else [0x7F800000, 0xFF800000, 0x7FC00000]),
+                        dtype=np.uint32)
+    pick = rng.random(t * m * n) < 0.05
+    c = np.where(pick, cspecial[rng.integers(0, 3, size=t * m * n)], c).astype(np.uint32).reshape(t, m, n)
+    kw = {kk: d[kk] for kk in KEYS}
+    got = t5.mma_batch(a, b, c, **kw)
+    aa = np.repeat(a, n, axis=1).reshape(-1, k)
+    bb = np.tile(bt, (1, m, 1)).reshape(-1, k)
+    want, st = oracle.mma_dot_batch(aa, bb, c.reshape(-1), **kw)
+    assert (st == 0).all()
+    words = got.reshape(-1)
+    assert ((words == 0x7FFFFFFF).sum() > 1000) and ((words == 0x7F800000).sum() > 1000) \
+        and ((words == 0xFF800000).sum() > 1000)  # every special outcome is reached
+    assert_words_equal(words, want, f"{desc} tiles with infinities and zeros vs oracle")
+
+
 @pytest.mark.parametrize("desc,k", [(dict(a_format="bf16"), 16), (dict(a_format="f16", d_type="f16"), 16)])
 def test_largest_staged_tiles_fast_equals_generic(desc, k):
     """The largest tile the specialised kernel stages (M=256 rows of A,
