@@ -55,8 +55,8 @@ NVFP4_CASES = 1 << 24
 E2E_RUNS = 3
 REF_DIR = REPO / "baseline" / "_ref"
 
-from tcgen05_b200.step import (CASES_PER_PATH, MATRIX_TILES, TILE_K, TILE_M, TILE_N,  # noqa: E402
-                               build_step, launcher, whole_step_macs)
+from tcgen05_b200.step import (CASES_PER_PATH, MATRIX_TILES, STEP_STREAMS, TILE_K, TILE_M, TILE_N,  # noqa: E402
+                               build_step, capture_step, launcher, stream_groups, whole_step_macs)
 
 
 def measured_peaks() -> tuple[dict, str]:
@@ -567,19 +567,19 @@ def run_ours(args) -> int:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize(dev)
-    # the step's launches, captured once in a CUDA graph: each timed step is
-    # one graph launch, so the host's launch rate never paces the GPU (the
-    # launches keep their programmatic dependencies inside the graph)
+    # the step's launches, captured once in a CUDA graph over STEP_STREAMS
+    # streams (groups of about equal time from one measured step): each
+    # timed step is one graph launch, so the host's launch rate never paces
+    # the GPU, and independent paths overlap one another's start and tail;
+    # within a stream the launches keep their programmatic dependencies
     graph, graph_note = None, "eager launches (graph capture unavailable)"
     try:
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g, capture_error_mode="thread_local"):
-            launch_c = launcher(lib, torch.cuda.current_stream(dev))
-            for item in items:
-                launch_c(item)
+        groups = stream_groups(per_launch_times(torch, stream, items, launch, steps=1), args.streams)
+        g = capture_step(torch, lib, dev, items, groups)
         g.replay()
         torch.cuda.synchronize(dev)
-        graph, graph_note = g, "one CUDA graph of the step's launches per step"
+        graph = g
+        graph_note = f"one CUDA graph of the step's launches per step, over {len(groups)} streams"
     except RuntimeError as exc:  # capture refused: time the launches eagerly
         print(f"bench: graph capture failed ({exc}); timing eager launches", file=sys.stderr)
         torch.cuda.synchronize(dev)
@@ -609,8 +609,13 @@ def run_ours(args) -> int:
         dist.barrier()
     clocks = sampler.stop()
     elapsed_ms = e0.elapsed_time(e1)
+    graph_words = [item.d.clone() for item in items] if graph is not None else None
     launch_ms = per_launch_times(torch, stream, items, launch)
+    # the timed graph's words equal those of the launches run one by one
+    graph_bad = 0 if graph_words is None else sum(int((w != item.d).sum()) for w, item in zip(graph_words, items))
+    del graph_words
     mismatches, sums = verify(torch, lib, stream, items)
+    mismatches += graph_bad
     nv = nvfp4_config(torch, dev, lib, stream, rank, world)
 
     # end to end through the public API on raw words in pinned host memory
@@ -726,8 +731,9 @@ def report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mis
         "dot_products_per_s": (46 * CASES_PER_PATH + MATRIX_TILES * TILE_M * TILE_N) * args.steps
                               / (elapsed_ms / 1e3),
         "mismatches": mismatches,
-        "mismatch_check": "every word of every launch against the generic kernel on the same inputs, and every "
-                          "end-to-end word against the timed launches' words",
+        "mismatch_check": "every word of every launch against the generic kernel on the same inputs, every word "
+                          "of the timed graph against the launches run one by one, and every end-to-end word "
+                          "against the timed launches' words",
         "gpu_launches": args.steps * len(items),
         "paths": paths,
         "kernel_ms_method": "an event between consecutive launches over 3 further steps, max over ranks",
@@ -887,6 +893,8 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-seconds", type=float, default=8.0,
                     help="wall seconds of the reference Python model's sample (all cores)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--streams", type=int, default=STEP_STREAMS,
+                    help="streams the step's graph spreads its launches over")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -173,6 +173,7 @@ constexpr uint32_t kLow16 = 0x80008000u;  // (-32768, -32768): below every raw e
 constexpr int kTileRows = 2;    // rows a thread evaluates together
 constexpr int kTileBlocks = 2;  // resident blocks per SM the register budget is set for
 constexpr int kTileThreads = 256;  // threads (columns) per block
+constexpr int kTileUnitsPerBlock = 4;  // row-block split target: units per resident block
 
 // 2**e as a double (-1022 <= e <= 1023).
 __device__ __forceinline__ double pow2(int e) { return __hiloint2double((e + 1023) << 20, 0); }
@@ -728,10 +729,12 @@ int launch_tiles(const t5e_batch& B, int floor_raw, cudaStream_t stream) {
   const uint64_t tiles = B.n / ((uint64_t)B.tile_m * (uint64_t)B.tile_n);
   const uint64_t cap = (uint64_t)sms * (uint64_t)per_sm;
   // split tiles into row blocks (of at least 16 rows, whole R-row steps)
-  // until there are about eight units per resident block, so that the last
-  // round of units leaves few blocks idle
+  // until there are about kTileUnitsPerBlock units per resident block, so
+  // that the last round of units leaves few blocks idle while each unit
+  // still amortises its staging over enough rows
   int split = 1;
-  while (tiles * (uint64_t)cblocks * (uint64_t)split < 8 * cap && B.tile_m % (2 * split * R) == 0 &&
+  while (tiles * (uint64_t)cblocks * (uint64_t)split < (uint64_t)kTileUnitsPerBlock * cap &&
+         B.tile_m % (2 * split * R) == 0 &&
          B.tile_m / (2 * split) >= 16)
     split *= 2;
   const uint64_t units = tiles * (uint64_t)cblocks * (uint64_t)split;

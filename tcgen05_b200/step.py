@@ -4,7 +4,10 @@ BF16 tiles of 128 x 256 x 16), sharded over the ranks of a job.
 
 ``build_step`` generates a rank's shard of every path (tcgen05_b200.sweep)
 and of the tiles in the kernels' layout; ``launcher`` returns the call that
-evaluates one of them through t5e_mma_dot_batch.  bench.py times these
+evaluates one of them through t5e_mma_dot_batch.  ``stream_groups`` and
+``capture_step`` record the step as one CUDA graph whose launches run on
+several streams: the paths are independent, so one launch's tail and the
+next one's start overlap with other paths' launches.  bench.py times these
 launches; ``python -m tcgen05_b200.step`` runs warm-up steps and one step, the
 command the launch-list profiles are taken with.
 """
@@ -86,6 +89,45 @@ def launcher(lib, stream):
             nat.check(rc, "t5e_mma_dot_batch " + item.name)
 
     return launch
+
+
+STEP_STREAMS = 4  # streams the step's graph spreads its launches over
+
+
+def stream_groups(times, streams: int = STEP_STREAMS) -> list[list[int]]:
+    """Indices of the step's launches split into `streams` groups of about
+    equal summed time: longest first, each to the least loaded group; each
+    group in launch order."""
+    load = [0.0] * streams
+    groups: list[list[int]] = [[] for _ in range(streams)]
+    for j in sorted(range(len(times)), key=lambda j: (-times[j], j)):
+        g = min(range(streams), key=lambda x: (load[x], x))
+        groups[g].append(j)
+        load[g] += times[j]
+    return [sorted(g) for g in groups if g]
+
+
+def capture_step(torch, lib, dev, items, groups):
+    """The step as one CUDA graph: each group's launches in order on a stream
+    of its own, forked from and joined back to the capturing stream."""
+    streams = [torch.cuda.Stream(dev) for _ in groups]
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, capture_error_mode="thread_local"):
+        cap = torch.cuda.current_stream(dev)
+        fork = torch.cuda.Event()
+        fork.record(cap)
+        joins = []
+        for s, grp in zip(streams, groups):
+            s.wait_event(fork)
+            launch = launcher(lib, s)
+            for j in grp:
+                launch(items[j])
+            done = torch.cuda.Event()
+            done.record(s)
+            joins.append(done)
+        for done in joins:
+            cap.wait_event(done)
+    return graph
 
 
 def whole_step_macs() -> int:

@@ -848,3 +848,13 @@ def test_step_launches_replay_from_a_cuda_graph():
     torch.cuda.synchronize(dev)
     for item, w in zip(items, want):
         assert torch.equal(item.d, w), item.name
+    # the bench's form: the same launches spread over streams in one graph
+    for item in items:
+        item.d.fill_(-1)
+    groups = step.stream_groups([float(len(it.name)) for it in items], 4)
+    g4 = step.capture_step(torch, lib, dev, items, groups)
+    for _ in range(2):
+        g4.replay()
+    torch.cuda.synchronize(dev)
+    for item, w in zip(items, want):
+        assert torch.equal(item.d, w), item.name

@@ -179,3 +179,17 @@ def test_gpu_every_path_at_full_size_matches_oracle():
             checked += count
     assert checked == total * len(PATHS)
     assert not bad, bad
+
+
+def test_step_stream_groups_cover_every_launch_once_and_balance():
+    from tcgen05_b200 import step
+
+    times = [5.0, 1.0, 1.0, 4.0, 2.0, 2.0, 3.0, 0.5]
+    groups = step.stream_groups(times, 3)
+    flat = sorted(j for g in groups for j in g)
+    assert flat == list(range(len(times)))
+    assert all(g == sorted(g) for g in groups)  # launch order kept within a stream
+    loads = [sum(times[j] for j in g) for g in groups]
+    assert max(loads) - min(loads) <= max(times)
+    assert step.stream_groups(times, 1) == [list(range(len(times)))]
+    assert len(step.stream_groups([1.0, 2.0], 4)) == 2  # no empty streams
