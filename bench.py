@@ -543,6 +543,7 @@ def run_ours(args) -> int:
 
     import tcgen05_b200 as t5
     from tcgen05_b200 import _native as nat
+    from tcgen05_b200 import workloads
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -557,7 +558,7 @@ def run_ours(args) -> int:
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     lib = nat.load()
     stream = torch.cuda.current_stream(dev)
-    items = build_step(torch, dev, rank, world)
+    items = build_step(torch, dev, rank, world, shard=args.shard)
     launch = launcher(lib, stream)
 
     def step():
@@ -637,8 +638,13 @@ def run_ours(args) -> int:
         dist.barrier()
     ceiling_s = host_copy_ceiling(torch, dev, stream, host)
 
-    # reductions: max of times over ranks, sums of counts and checksums
-    names = [item.name for item in items]
+    # reductions over the job's launches (every path and the tiles, whichever
+    # rank evaluates them): max of times over ranks, sums of counts and
+    # checksums (a rank that does not evaluate a path adds 0)
+    names = [spec.name for spec in workloads.validation_paths()] + ["matrix-bf16"]
+    ms_by_name = {item.name: ms for item, ms in zip(items, launch_ms)}
+    launch_ms = [ms_by_name.get(nm, 0.0) for nm in names]
+    launches = len(items)
     if world > 1:
         t = torch.tensor([elapsed_ms, e2e_s, ceiling_s, nv["ms"]["nvfp4-k64"], nv["ms"]["nvfp4-sparse-k128"],
                           *launch_ms], dtype=torch.float64, device=dev)
@@ -646,18 +652,19 @@ def run_ours(args) -> int:
         elapsed_ms, e2e_s, ceiling_s = float(t[0]), float(t[1]), float(t[2])
         nv["ms"] = {"nvfp4-k64": float(t[3]), "nvfp4-sparse-k128": float(t[4])}
         launch_ms = [float(x) for x in t[5:]]
-        cnt = torch.tensor([mismatches, e2e_bad, nv["mismatches"], h2d, d2h, *[sums[nm] for nm in names]],
-                           dtype=torch.int64, device=dev)
+        cnt = torch.tensor([mismatches, e2e_bad, nv["mismatches"], h2d, d2h, launches,
+                            *[sums.get(nm, 0) for nm in names]], dtype=torch.int64, device=dev)
         dist.all_reduce(cnt, op=dist.ReduceOp.SUM)
-        mismatches, e2e_bad, nv["mismatches"], h2d, d2h = (int(x) for x in cnt[:5].tolist())
-        sums = {nm: int(v) for nm, v in zip(names, cnt[5:].tolist())}
+        mismatches, e2e_bad, nv["mismatches"], h2d, d2h, launches = (int(x) for x in cnt[:6].tolist())
+        sums = {nm: int(v) for nm, v in zip(names, cnt[6:].tolist())}
     step_macs = whole_step_macs()  # the configuration's work, however it is split over the ranks
     value = step_macs * args.steps / (elapsed_ms / 1e3)
     e2e_value = step_macs / e2e_s
 
     if rank == 0:
-        line = report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mismatches + e2e_bad, sums,
-                           nv, clocks, e2e_value, e2e_runs, e2e_s, ceiling_s, h2d, d2h, torch, lib, stream)
+        line = report_line(args, world, items, names, launches, elapsed_ms, launch_ms, value, step_macs,
+                           mismatches + e2e_bad, sums, nv, clocks, e2e_value, e2e_runs, e2e_s, ceiling_s, h2d, d2h,
+                           torch, lib, stream)
         line["timed_launches"] = graph_note
         if world == 1 and not args.no_cpu_baseline:
             line.update(cpu_baselines(items, host, args.cpu_seconds))
@@ -668,27 +675,53 @@ def run_ours(args) -> int:
     return 0 if mismatches + e2e_bad == 0 else 1
 
 
-def report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mismatches, sums, nv, clocks,
-                e2e_value, e2e_runs, e2e_s, ceiling_s, h2d, d2h, torch, lib, stream) -> dict:
+def launch_table(world, items, names, shard) -> dict:
+    """Kernel and algorithmic bytes of each of the job's launches as one rank
+    runs it: a whole path (``shard="paths"``) or a rank's share of its cases,
+    and a rank's share of the tiles (all ranks' shares are equal within one
+    tile, so this rank's stands for all)."""
+    from tcgen05_b200 import sweep, workloads
+    from tcgen05_b200.step import kernel_of
+
+    specs = {s.name: s for s in workloads.validation_paths()}
+    own = {item.name: item for item in items}
+    table = {}
+    for nm in names:
+        if nm in own:
+            table[nm] = (own[nm].kernel, own[nm].bytes)
+        else:
+            lo, hi = (0, CASES_PER_PATH) if shard == "paths" else sweep.shard(CASES_PER_PATH, 0, world)
+            table[nm] = (kernel_of(specs[nm]), sweep.path_work(specs[nm], hi - lo)[1])
+    return table
+
+
+def report_line(args, world, items, names, launches, elapsed_ms, launch_ms, value, step_macs, mismatches, sums, nv,
+                clocks, e2e_value, e2e_runs, e2e_s, ceiling_s, h2d, d2h, torch, lib, stream) -> dict:
     from tcgen05_b200 import sweep, workloads
 
     peaks, peak_kind = measured_peaks()
     hbm = peaks["hbm_gbs"]
     specs = {s.name: s for s in workloads.validation_paths()}
+    table = launch_table(world, items, names, args.shard)
     paths = {}
-    for item, ms in zip(items, launch_ms):
-        job_macs = (sweep.path_work(specs[item.name], CASES_PER_PATH)[0] if item.name in specs
+    for nm, ms in zip(names, launch_ms):
+        job_macs = (sweep.path_work(specs[nm], CASES_PER_PATH)[0] if nm in specs
                     else MATRIX_TILES * TILE_M * TILE_N * TILE_K)
-        gbs = item.bytes / (ms / 1e3) / 1e9  # this rank's shard
-        paths[item.name] = {"kernel": item.kernel, "ms_per_launch": ms, "element_macs_per_s": job_macs / (ms / 1e3),
-                            "hbm_frac": gbs / hbm, "checksum": f"{sums[item.name] & 0xFFFFFFFFFFFFFFFF:016x}"}
-    dom = max(range(len(items)), key=lambda j: launch_ms[j])
-    di, dms = items[dom], launch_ms[dom]
-    achieved = di.bytes / (dms / 1e3) / 1e9
-    tag = f"{di.kernel} {di.name}"
-    traffic, traffic_state = profiled_figure("traffic_bytes_per_launch", tag, di.kernel)
+        kernel, nbytes = table[nm]
+        gbs = nbytes / (ms / 1e3) / 1e9  # the launch as one rank runs it
+        paths[nm] = {"kernel": kernel, "ms_per_launch": ms, "element_macs_per_s": job_macs / (ms / 1e3),
+                     "hbm_frac": gbs / hbm, "checksum": f"{sums[nm] & 0xFFFFFFFFFFFFFFFF:016x}"}
+    dom = max(range(len(names)), key=lambda j: launch_ms[j])
+    dname, dms = names[dom], launch_ms[dom]
+    dkernel, dbytes = table[dname]
+    achieved = dbytes / (dms / 1e3) / 1e9
+    tag = f"{dkernel} {dname}"
+    traffic, traffic_state = profiled_figure("traffic_bytes_per_launch", tag, dkernel)
+    # the ncu figures are for the full tile configuration on one GPU; a rank's
+    # share of the tiles (or of a path's cases) does 1/N of it
+    per_rank = world if (dname == "matrix-bf16" or args.shard == "cases") else 1
     if traffic is not None:
-        traffic /= world  # the ncu figure is for the full configuration on one GPU; a shard moves 1/N of it
+        traffic /= per_rank
     peak_issue = issue_peaks(torch, lib, stream)
     int_pipe = {"alu_peak_warp_inst_per_s": peak_issue["alu"], "fma_peak_warp_inst_per_s": peak_issue["fma"],
                 "fp64_peak_warp_inst_per_s": peak_issue["fp64"],
@@ -696,12 +729,11 @@ def report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mis
                           "ncu summary, used only while its source stamp matches the kernel's source"}
     fracs = {"hbm": achieved / hbm}
     for pipe in ("alu", "fma", "fp64"):
-        per_launch, state = profiled_figure(f"{pipe}_warp_inst_per_launch", tag, di.kernel)
+        per_launch, state = profiled_figure(f"{pipe}_warp_inst_per_launch", tag, dkernel)
         int_pipe[f"kernel_{pipe}_warp_inst_per_launch"] = per_launch
         int_pipe[f"{pipe}_figure"] = state
         if per_launch is not None:
-            # the ncu figure is for the full configuration on one GPU; a shard does 1/N of it
-            fracs[pipe] = per_launch / world / (dms / 1e3) / peak_issue[pipe]
+            fracs[pipe] = per_launch / per_rank / (dms / 1e3) / peak_issue[pipe]
             int_pipe[f"{pipe}_frac"] = fracs[pipe]
     step_bytes = sum(item.bytes for item in items)
     nv_dense = NVFP4_CASES * 64 / (nv["ms"]["nvfp4-k64"] / 1e3)
@@ -726,21 +758,23 @@ def report_line(args, world, items, elapsed_ms, launch_ms, value, step_macs, mis
                    "cases_per_path": CASES_PER_PATH, "paths": 46, "matrix_tiles": MATRIX_TILES,
                    "element_macs_per_step": step_macs,
                    "l2": f"every batch read once per step; {step_bytes / 1e6:.0f} MB of inputs and outputs per "
-                         f"step on each GPU > 126 MB L2",
-                   "parallelism": f"dp{world} (case shards)" if world > 1 else "single GPU"},
+                         f"step on rank 0's GPU > 126 MB L2",
+                   "parallelism": (("whole paths per rank by measured cost, tile shards" if args.shard == "paths"
+                                    else "case shards of every path, tile shards") + f" over {world} GPUs")
+                                  if world > 1 else "single GPU"},
         "dot_products_per_s": (46 * CASES_PER_PATH + MATRIX_TILES * TILE_M * TILE_N) * args.steps
                               / (elapsed_ms / 1e3),
         "mismatches": mismatches,
         "mismatch_check": "every word of every launch against the generic kernel on the same inputs, every word "
                           "of the timed graph against the launches run one by one, and every end-to-end word "
                           "against the timed launches' words",
-        "gpu_launches": args.steps * len(items),
+        "gpu_launches": args.steps * launches,
         "paths": paths,
         "kernel_ms_method": "an event between consecutive launches over 3 further steps, max over ranks",
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s", "frac": achieved / hbm,
                      "traffic": traffic, "traffic_figure": traffic_state,
                      "kernel": tag, "peak_source": f"{peak_kind} hbm_gbs (burst copy)",
-                     "algorithmic_bytes_per_launch": di.bytes, "ms_per_launch": dms,
+                     "algorithmic_bytes_per_launch": dbytes, "ms_per_launch": dms,
                      "share_of_step": dms / sum(launch_ms), "int_pipe": int_pipe,
                      "binds": max(fracs, key=fracs.get),
                      "step": {"algorithmic_bytes": step_bytes, "gbs": step_bytes / (elapsed_ms / args.steps / 1e3) / 1e9,
@@ -895,6 +929,8 @@ def main(argv=None) -> int:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--streams", type=int, default=STEP_STREAMS,
                     help="streams the step's graph spreads its launches over")
+    ap.add_argument("--shard", choices=("paths", "cases"), default="paths",
+                    help="over N GPUs: whole paths per rank (by measured cost) or a share of every path's cases")
     args = ap.parse_args(argv)
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")

@@ -54,16 +54,60 @@ class Launch:
         self.first_case = first_case  # global index of this shard's first case
 
 
+# Microseconds per launch of each path at 1,000,000 cases on one B200 (the
+# bench step's per-launch events, SM clock 1965 MHz): the weights by which
+# whole paths are spread over the ranks of a job.
+PATH_COST_US = {"dense-tf32": 27.1, "dense-bf16": 33.6, "dense-f16": 33.2, "dense-e4m3": 33.4,
+                "dense-e5m2": 31.7, "dense-e2m3": 36.2, "dense-e3m2": 36.2, "dense-e2m1": 34.8,
+                "i8-u8-u8-wrap": 18.5, "i8-s8-u8-wrap": 18.2, "i8-u8-s8-wrap": 18.7, "i8-s8-s8-wrap": 18.4,
+                "i8-u8-u8-saturate": 18.4, "i8-s8-u8-saturate": 18.5, "i8-u8-s8-saturate": 18.8,
+                "i8-s8-s8-saturate": 18.4, "dense-mx-e4m3": 35.9, "dense-mx-e5m2": 35.0, "dense-mx-e2m3": 36.2,
+                "dense-mx-e3m2": 36.8, "dense-mx-e2m1": 36.5, "dense-mxf4": 28.7, "dense-mxf4nvf4-2x": 28.3,
+                "dense-mxf4nvf4-4x": 28.7, "dense-mxf4nvf4-4x-ue4m3": 24.2, "sparse-tf32": 29.3,
+                "sparse-bf16": 38.9, "sparse-f16": 39.6, "sparse-fp8": 45.4, "sparse-e5m2": 41.5,
+                "sparse-e2m3": 47.2, "sparse-e3m2": 46.5, "sparse-e2m1": 43.7, "sparse-nvfp4": 31.7,
+                "sparse-mx-e4m3": 47.1, "sparse-mx-e5m2": 44.4, "sparse-mx-e2m3": 46.0, "sparse-mx-e3m2": 46.1,
+                "sparse-mx-e2m1": 41.3, "sparse-mxf4": 33.1, "sparse-mxf4nvf4-2x": 32.8, "sparse-mxf4nvf4-4x": 34.8,
+                "sparse-mxf4nvf4-4x-ue4m3": 32.8, "mixed-e4m3-e2m1-f32": 33.1, "mixed-e2m1-e4m3-f16": 33.5,
+                "dense-nvfp4": 24.6}
+DEFAULT_PATH_COST_US = 40.0
+
+
+def path_owners(world: int) -> dict[str, int]:
+    """The rank that evaluates each whole path of the sweep: longest paths
+    first, each to the least loaded rank (ties to the lower rank), so every
+    rank computes the same assignment without communicating."""
+    from . import workloads
+
+    names = [s.name for s in workloads.validation_paths()]
+    cost = {n: PATH_COST_US.get(n, DEFAULT_PATH_COST_US) for n in names}
+    load = [0.0] * world
+    owners = {}
+    for n in sorted(names, key=lambda n: (-cost[n], names.index(n))):
+        r = min(range(world), key=lambda x: (load[x], x))
+        owners[n] = r
+        load[r] += cost[n]
+    return owners
+
+
 def build_step(torch, dev, rank: int, world: int, *, cases_per_path: int = CASES_PER_PATH,
-               tiles: int = MATRIX_TILES) -> list[Launch]:
-    """This rank's shard of every path and of the matrix tiles, generated in
-    HBM in the kernels' layout (smaller steps for profiling keep the same
-    distributions)."""
+               tiles: int = MATRIX_TILES, shard: str = "paths") -> list[Launch]:
+    """This rank's part of the step, generated in HBM in the kernels' layout
+    (smaller steps for profiling keep the same distributions): the matrix
+    tiles split evenly, and the sweep either as whole paths per rank
+    (``shard="paths"``, ``path_owners``: every launch keeps its full size, as
+    the reference's validation runner gives whole paths to devices) or as a
+    contiguous share of every path's cases (``shard="cases"``)."""
     from . import sweep, workloads
 
+    if shard not in ("paths", "cases"):
+        raise ValueError(f"unknown shard mode {shard!r}")
     items = []
-    lo, hi = sweep.shard(cases_per_path, rank, world)
+    owners = path_owners(world) if shard == "paths" else None
+    lo, hi = (0, cases_per_path) if shard == "paths" else sweep.shard(cases_per_path, rank, world)
     for spec in workloads.validation_paths():
+        if owners is not None and owners[spec.name] != rank:
+            continue
         model, db = sweep.device_batch(spec, lo, hi - lo, cases_per_path, dev)
         macs, nbytes = sweep.path_work(spec, db.n, model)
         d = torch.empty(db.n, dtype=torch.int32, device=dev)

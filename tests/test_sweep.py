@@ -193,3 +193,22 @@ def test_step_stream_groups_cover_every_launch_once_and_balance():
     assert max(loads) - min(loads) <= max(times)
     assert step.stream_groups(times, 1) == [list(range(len(times)))]
     assert len(step.stream_groups([1.0, 2.0], 4)) == 2  # no empty streams
+
+
+def test_path_owners_cover_every_path_once_with_balanced_cost():
+    """Whole-path sharding: every rank computes the same assignment, each
+    path has one owner, and no rank carries more than the average plus one
+    path's cost."""
+    from tcgen05_b200 import step, workloads
+
+    names = [s.name for s in workloads.validation_paths()]
+    assert set(step.PATH_COST_US) == set(names)
+    assert step.path_owners(1) == {n: 0 for n in names}
+    for world in (2, 3, 4, 8):
+        owners = step.path_owners(world)
+        assert owners == step.path_owners(world)
+        assert set(owners) == set(names) and set(owners.values()) == set(range(world))
+        load = [0.0] * world
+        for n, r in owners.items():
+            load[r] += step.PATH_COST_US[n]
+        assert max(load) <= sum(load) / world + max(step.PATH_COST_US.values())
