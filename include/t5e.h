@@ -225,7 +225,10 @@ int t5e_mma_dot_batch_staged_async(const t5e_model* model, const t5e_batch* host
  * 256 bytes) do not fit in the array is rejected with T5E_ERR_INVALID and a
  * message in t5e_last_error().  Calls no allocator.  The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress, with
- * that device current); make it before any stream capture.  Every call on a
+ * that device current).  Because every call synchronizes `stream`, no call
+ * can be captured into a CUDA graph: on a capturing stream the call returns
+ * T5E_ERR_INVALID before queuing anything (the capture stays valid).  Every
+ * call on a
  * device shares the one array: calls that overlap in time on that device, on
  * any streams or host threads, overwrite each other's data. */
 int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch* host, void* stream);

@@ -13,8 +13,8 @@
 //
 // Host code cannot use the array's name as a device address, so the
 // device address is looked up once per device with cudaGetSymbolAddress
-// (with that device current) and kept.  The first call on a device does that
-// look-up; make it before any stream capture.
+// (with that device current) and kept.  Every call synchronizes its stream,
+// so a call on a capturing stream is refused before anything is queued.
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -97,6 +97,18 @@ extern "C" int t5e_mma_dot_batch_noalloc(const t5e_model* model, const t5e_batch
                   (unsigned long long)need, (unsigned long long)cap);
     set_cuda_error(message, cudaErrorInvalidValue);
     return T5E_ERR_INVALID;
+  }
+  // every call ends by synchronizing the stream, which a stream capture does
+  // not allow: refuse a capturing stream before anything is queued
+  {
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &capture) != cudaSuccess ||
+        capture != cudaStreamCaptureStatusNone) {
+      set_cuda_error("t5e_mma_dot_batch_noalloc: the stream is capturing (or its state is unknown); the call "
+                     "synchronizes its stream and cannot be part of a CUDA graph",
+                     cudaErrorStreamCaptureUnsupported);
+      return T5E_ERR_INVALID;
+    }
   }
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);

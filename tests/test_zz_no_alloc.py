@@ -199,3 +199,29 @@ def test_header_and_python_agree_on_the_array_size():
     text = (Path(__file__).resolve().parents[1] / "include" / "t5e.h").read_text()
     m = re.search(r"#define T5E_NOALLOC_STAGE_BYTES \((\d+)u \* 1024u \* 1024u\)", text)
     assert m and int(m.group(1)) * 1024 * 1024 == nat.NOALLOC_STAGE_BYTES
+
+
+@pytest.mark.gpu
+def test_call_on_a_capturing_stream_is_refused_and_the_capture_survives():
+    """The entry point synchronizes its stream, which a capture forbids: on a
+    capturing stream it returns T5E_ERR_INVALID without queuing anything, and
+    the capture (here of a plain tensor fill) still completes and replays."""
+    import torch
+
+    cases = workloads.path_cases(PATHS["dense-e4m3"], 256, seed=7)
+    desc, hb = _host_batch(cases)
+    d = torch.full((hb.n,), -1, dtype=torch.int32)
+    bs = runtime.make_batch_struct(hb, d, None)
+    lib = nat.load()
+    x = torch.zeros(16, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        stream = torch.cuda.current_stream().cuda_stream
+        rc = lib.t5e_mma_dot_batch_noalloc(ctypes.byref(desc), ctypes.byref(bs), ctypes.c_void_p(stream))
+        x.fill_(3.0)
+    assert rc == nat.ERR_INVALID
+    assert "capturing" in nat.load().t5e_last_error().decode()
+    g.replay()
+    torch.cuda.synchronize()
+    assert float(x.sum()) == 48.0
+    assert int((d == -1).sum()) == hb.n  # nothing was written
