@@ -339,6 +339,36 @@ def host_step(torch, dev, items) -> list[tuple]:
     return out
 
 
+def e2e_items(torch, items, rank: int, world: int, shard: str) -> list:
+    """The launches a rank evaluates end to end: its share of the tiles and,
+    over N GPUs with whole-path sharding, the paths ``host_path_owners`` gives
+    it (by host bytes, not GPU time); otherwise its own launches' paths.
+    Paths it did not time are stood in for by their name, first case and
+    result shape."""
+    from types import SimpleNamespace
+
+    from tcgen05_b200 import workloads
+    from tcgen05_b200.step import host_path_owners
+
+    if world == 1 or shard != "paths":
+        return items
+    owners = host_path_owners(world)
+    out = [SimpleNamespace(name=s.name, first_case=0,
+                           d=torch.empty(CASES_PER_PATH, dtype=torch.int32, device="meta"))
+           for s in workloads.validation_paths() if owners[s.name] == rank]
+    return out + [item for item in items if item.name == "matrix-bf16"]
+
+
+def result_words_checksum(torch, first_case: int, res) -> int:
+    """The order-independent checksum of (global case index, word) pairs of
+    result words in host memory (the one ``verify`` forms on the device)."""
+    from tcgen05_b200 import sweep
+
+    words = res.view(-1).to(torch.int64) & 0xFFFFFFFF
+    idx = torch.arange(first_case, first_case + words.numel(), dtype=torch.int64)
+    return sweep.result_checksum(torch, idx, words)
+
+
 def copy_bytes(host) -> tuple[int, int]:
     """(host-to-device, device-to-host) bytes of one end-to-end step."""
     h2d = d2h = 0
@@ -619,11 +649,18 @@ def run_ours(args) -> int:
     mismatches += graph_bad
     nv = nvfp4_config(torch, dev, lib, stream, rank, world)
 
-    # end to end through the public API on raw words in pinned host memory
-    host = host_step(torch, dev, items)
+    # end to end through the public API on raw words in pinned host memory;
+    # over N GPUs each rank takes whole paths by host bytes (the host link
+    # bounds this step) and its share of the tiles
+    host = host_step(torch, dev, e2e_items(torch, items, rank, world, args.shard))
     h2d, d2h = copy_bytes(host)
     e2e_step(t5, host)  # once untimed: the allocator then holds the buffers the timed runs need
-    e2e_bad = sum(int((res.view(-1) != item.d.cpu().view(-1)).sum()) for item, _, _, _, res in host)
+    # tile words against the timed launches' directly; each path's words by
+    # their checksum, compared with the timed launches' after the reduction
+    e2e_bad = sum(int((res.view(-1) != item.d.cpu().view(-1)).sum())
+                  for item, kind, _, _, res in host if kind == "tiles")
+    e2e_sums = {item.name: result_words_checksum(torch, item.first_case, res)
+                for item, kind, _, _, res in host if kind == "cases"}
     e2e_runs = []
     for _ in range(E2E_RUNS):
         if world > 1:
@@ -645,7 +682,14 @@ def run_ours(args) -> int:
     ms_by_name = {item.name: ms for item, ms in zip(items, launch_ms)}
     launch_ms = [ms_by_name.get(nm, 0.0) for nm in names]
     launches = len(items)
+    by_rank = None
     if world > 1:
+        # each rank's end-to-end time, copy ceiling and host bytes, in its own slot
+        slots = torch.zeros(world, 3, dtype=torch.float64, device=dev)
+        slots[rank] = torch.tensor([e2e_s, ceiling_s, float(h2d)], dtype=torch.float64)
+        dist.all_reduce(slots, op=dist.ReduceOp.SUM)
+        by_rank = {"e2e_s": slots[:, 0].tolist(), "host_copy_ceiling_s": slots[:, 1].tolist(),
+                   "h2d_bytes": [int(x) for x in slots[:, 2].tolist()]}
         t = torch.tensor([elapsed_ms, e2e_s, ceiling_s, nv["ms"]["nvfp4-k64"], nv["ms"]["nvfp4-sparse-k128"],
                           *launch_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -653,10 +697,14 @@ def run_ours(args) -> int:
         nv["ms"] = {"nvfp4-k64": float(t[3]), "nvfp4-sparse-k128": float(t[4])}
         launch_ms = [float(x) for x in t[5:]]
         cnt = torch.tensor([mismatches, e2e_bad, nv["mismatches"], h2d, d2h, launches,
-                            *[sums.get(nm, 0) for nm in names]], dtype=torch.int64, device=dev)
+                            *[sums.get(nm, 0) for nm in names], *[e2e_sums.get(nm, 0) for nm in names]],
+                           dtype=torch.int64, device=dev)
         dist.all_reduce(cnt, op=dist.ReduceOp.SUM)
         mismatches, e2e_bad, nv["mismatches"], h2d, d2h, launches = (int(x) for x in cnt[:6].tolist())
-        sums = {nm: int(v) for nm, v in zip(names, cnt[6:].tolist())}
+        sums = {nm: int(v) for nm, v in zip(names, cnt[6:6 + len(names)].tolist())}
+        e2e_sums = {nm: int(v) for nm, v in zip(names, cnt[6 + len(names):].tolist())}
+    # a path whose end-to-end words differ from the timed launches' counts as one mismatch
+    e2e_bad += sum(1 for nm in names if nm != "matrix-bf16" and e2e_sums.get(nm, 0) != sums.get(nm, 0))
     step_macs = whole_step_macs()  # the configuration's work, however it is split over the ranks
     value = step_macs * args.steps / (elapsed_ms / 1e3)
     e2e_value = step_macs / e2e_s
@@ -666,6 +714,8 @@ def run_ours(args) -> int:
                            mismatches + e2e_bad, sums, nv, clocks, e2e_value, e2e_runs, e2e_s, ceiling_s, h2d, d2h,
                            torch, lib, stream)
         line["timed_launches"] = graph_note
+        if by_rank is not None:
+            line["e2e"]["by_rank"] = by_rank
         if world == 1 and not args.no_cpu_baseline:
             line.update(cpu_baselines(items, host, args.cpu_seconds))
         print(json.dumps(line), flush=True)
@@ -766,8 +816,9 @@ def report_line(args, world, items, names, launches, elapsed_ms, launch_ms, valu
                               / (elapsed_ms / 1e3),
         "mismatches": mismatches,
         "mismatch_check": "every word of every launch against the generic kernel on the same inputs, every word "
-                          "of the timed graph against the launches run one by one, and every end-to-end word "
-                          "against the timed launches' words",
+                          "of the timed graph against the launches run one by one, the end-to-end tile words "
+                          "against the timed launches' words, and each path's end-to-end words by their checksum "
+                          "against the timed launches' (a differing path counts one)",
         "gpu_launches": args.steps * launches,
         "paths": paths,
         "kernel_ms_method": "an event between consecutive launches over 3 further steps, max over ranks",
@@ -788,7 +839,9 @@ def report_line(args, world, items, names, launches, elapsed_ms, launch_ms, valu
                 "runs_s": e2e_runs, "reported": "median of the runs, max over ranks",
                 "host_copy_ceiling_s": ceiling_s, "frac_of_host_copy_ceiling": ceiling_s / e2e_s,
                 "calls": "mma_dot_batch per path and mma_batch for the tiles, raw uint32 container words in pinned "
-                         "host memory, pinned out, wait=False, at most four calls in flight"},
+                         "host memory, pinned out, wait=False, at most four calls in flight",
+                "assignment": ("whole paths per rank by host bytes, tile shares" if world > 1 and args.shard == "paths"
+                               else "the timed launches' cases")},
         "clocks": clocks,
     }
 

@@ -90,6 +90,41 @@ def path_owners(world: int) -> dict[str, int]:
     return owners
 
 
+def path_host_bytes(spec) -> int:
+    """Host bytes per case of a path through the public API on raw words, as
+    the bench's end-to-end step moves them: A and B container words (A at
+    logical K for sparse paths), C, the scale bytes and metadata words the
+    generator produces, and the 32-bit result word."""
+    import numpy as np
+
+    from . import sweep
+
+    g = sweep.generate(spec, 0, 1, 2, np)
+    per = 4 * (g["a"].shape[1] + g["b"].shape[1]) + (2 if spec.descriptor["d_type"] == "f16" else 4) + 4
+    if g["scale_a"] is not None:
+        per += g["scale_a"].shape[1] + g["scale_b"].shape[1]
+    if g["meta"] is not None:
+        per += 4 * g["meta"].shape[1]
+    return per
+
+
+def host_path_owners(world: int) -> dict[str, int]:
+    """``path_owners`` weighted by host bytes instead of GPU time: for a step
+    through the public API from host memory, which the host link bounds."""
+    from . import workloads
+
+    specs = workloads.validation_paths()
+    names = [s.name for s in specs]
+    cost = {s.name: path_host_bytes(s) for s in specs}
+    load = [0] * world
+    owners = {}
+    for n in sorted(names, key=lambda n: (-cost[n], names.index(n))):
+        r = min(range(world), key=lambda x: (load[x], x))
+        owners[n] = r
+        load[r] += cost[n]
+    return owners
+
+
 def build_step(torch, dev, rank: int, world: int, *, cases_per_path: int = CASES_PER_PATH,
                tiles: int = MATRIX_TILES, shard: str = "paths") -> list[Launch]:
     """This rank's part of the step, generated in HBM in the kernels' layout

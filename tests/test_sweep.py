@@ -212,3 +212,21 @@ def test_path_owners_cover_every_path_once_with_balanced_cost():
         for n, r in owners.items():
             load[r] += step.PATH_COST_US[n]
         assert max(load) <= sum(load) / world + max(step.PATH_COST_US.values())
+
+
+def test_host_path_owners_balance_host_bytes():
+    """The end-to-end step deals whole paths by host bytes: every path has
+    one owner, and no rank carries more than the average plus one path."""
+    from tcgen05_b200 import step, workloads
+
+    specs = workloads.validation_paths()
+    per = {s.name: step.path_host_bytes(s) for s in specs}
+    assert per["dense-tf32"] == 4 * (8 + 8) + 4 + 4
+    assert per["sparse-nvfp4"] == 4 * (128 + 128) + 4 + 4 + 4 + 4 + 8
+    for world in (1, 2, 8):
+        owners = step.host_path_owners(world)
+        assert set(owners) == set(per)
+        load = [0] * world
+        for n, r in owners.items():
+            load[r] += per[n]
+        assert max(load) <= sum(load) / world + max(per.values())
