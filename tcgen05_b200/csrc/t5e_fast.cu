@@ -577,7 +577,13 @@ struct MxUnit {  // u = (minimum raw exponent) - (fraction bits)
 
 constexpr int kMxThreads = 1024;  // one block per SM, 64 registers a thread
 constexpr int kMxWarps = kMxThreads / 32;
-constexpr int kMxLutBytes = 64 * 256;  // entry of (a, b) at byte (a << 8) | (b << 2)
+// The table is held in four replicas, interleaved: entry (a, b) of replica r
+// at byte (a << 10) | (b << 4) | (r << 2).  Lane l reads replica l % 4, so a
+// quarter of the warp's lanes shares a set of 8 banks that no other quarter
+// touches (a bank is (b % 8) * 4 + r), and random code pairs collide in a
+// bank about a third less often than with one copy over 32 banks.
+constexpr int kMxReplicas = 4;
+constexpr int kMxLutBytes = 64 * 256 * kMxReplicas;
 constexpr int kMxQueue = 64;           // per-warp queue of case indices (< 32 left over + 32 new)
 constexpr int kMxExpBias = 64;         // raw exponent bias of the entries' top byte
 
@@ -593,15 +599,19 @@ __device__ void build_mx_lut(uint32_t* lut) {
       const int nb = db.m * (1 << (db.ve - MxUnit<BF>::value));
       e = ((uint32_t)(da.re + db.re + kMxExpBias) << 24) | ((uint32_t)(na * nb) & 0xFFFFFFu);
     }
-    lut[ca * 64 + cb] = e;
+#pragma unroll
+    for (int r = 0; r < kMxReplicas; ++r) lut[((ca * 64 + cb) * kMxReplicas) + r] = e;
   }
 }
 
-// The four entries of code word pair (ca, cb << 2): byte addresses
-// (ca_j << 8) | (cb_j << 2) formed two at a time by one byte permute.
-__device__ __forceinline__ void mx_entries(const uint8_t* smem, uint32_t ca, uint32_t cb4, uint32_t (&e)[4]) {
-  const uint32_t p01 = __byte_perm(ca, cb4, 0x1504u);  // [cb0, ca0, cb1, ca1]
-  const uint32_t p23 = __byte_perm(ca, cb4, 0x3726u);  // [cb2, ca2, cb3, ca3]
+// The four entries of code word pair (ca, cb << 2) from this lane's replica:
+// (ca_j << 8) | (cb_j << 2) formed two at a time by one byte permute (below
+// 2**14 in each 16-bit half), then times four plus the replica offset rr2
+// (((lane % 4) << 2) in both halves), which carries into neither half.
+__device__ __forceinline__ void mx_entries(const uint8_t* smem, uint32_t ca, uint32_t cb4, uint32_t rr2,
+                                           uint32_t (&e)[4]) {
+  const uint32_t p01 = __byte_perm(ca, cb4, 0x1504u) * 4u + rr2;  // [cb0, ca0, cb1, ca1]
+  const uint32_t p23 = __byte_perm(ca, cb4, 0x3726u) * 4u + rr2;  // [cb2, ca2, cb3, ca3]
   e[0] = *reinterpret_cast<const uint32_t*>(smem + (p01 & 0xFFFFu));
   e[1] = *reinterpret_cast<const uint32_t*>(smem + (p01 >> 16));
   e[2] = *reinterpret_cast<const uint32_t*>(smem + (p23 & 0xFFFFu));
@@ -621,6 +631,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_kernel(const t5e_batch B) {
   constexpr int kU = MxUnit<AF>::value + MxUnit<BF>::value;
   const uint32_t lane = threadIdx.x & 31u;
   const uint32_t lt_mask = (1u << lane) - 1u;
+  const uint32_t rr2 = ((lane % kMxReplicas) << 2) * 0x00010001u;  // this lane's replica, both halves
   uint32_t* queue = reinterpret_cast<uint32_t*>(smem + kMxLutBytes) + (threadIdx.x >> 5) * kMxQueue;
   const uint8_t* A = static_cast<const uint8_t*>(B.a);
   const uint8_t* Bm = static_cast<const uint8_t*>(B.b);
@@ -652,7 +663,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_kernel(const t5e_batch B) {
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
         uint32_t e[4];
-        mx_entries(smem, ca[w], cb[w] << 2, e);  // codes below 64: << 2 stays in each byte
+        mx_entries(smem, ca[w], cb[w] << 2, rr2, e);  // codes below 64: << 2 stays in each byte
         sum += (e[0] + e[1]) + (e[2] + e[3]);
         emax = max(max(emax, max(e[0], e[1])), max(e[2], e[3]));
       }
@@ -706,7 +717,7 @@ __global__ void __launch_bounds__(kMxThreads, 1) mx_kernel(const t5e_batch B) {
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
         uint32_t e[4];
-        mx_entries(smem, ca[w], cb[w] << 2, e);
+        mx_entries(smem, ca[w], cb[w] << 2, rr2, e);
 #pragma unroll
         for (int t = 0; t < 4; ++t) {
           const int32_t p = (int32_t)(e[t] << 8) >> 8;
@@ -727,6 +738,8 @@ template <int AF, int BF, int SP>
 int launch_mx(const t5e_batch& B, cudaStream_t stream) {
   auto kern = mx_kernel<AF, BF, SP>;
   const int smem = kMxLutBytes + kMxWarps * kMxQueue * 4;
+  const int rc = raise_smem_limit<mx_kernel<AF, BF, SP>>(smem, "mx_kernel attribute");  // above 48 KB
+  if (rc != T5E_OK) return rc;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
