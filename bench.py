@@ -339,12 +339,12 @@ def host_step(torch, dev, items) -> list[tuple]:
     return out
 
 
-def e2e_items(torch, items, rank: int, world: int, shard: str) -> list:
+def e2e_items(torch, items, rank: int, world: int, shard: str, rates=None, base_bytes: float = 0.0) -> list:
     """The launches a rank evaluates end to end: its share of the tiles and,
     over N GPUs with whole-path sharding, the paths ``host_path_owners`` gives
-    it (by host bytes, not GPU time); otherwise its own launches' paths.
-    Paths it did not time are stood in for by their name, first case and
-    result shape."""
+    it (by host bytes, not GPU time, over each rank's host-link rate when
+    ``rates`` holds them); otherwise its own launches' paths.  Paths it did
+    not time are stood in for by their name, first case and result shape."""
     from types import SimpleNamespace
 
     from tcgen05_b200 import workloads
@@ -352,7 +352,7 @@ def e2e_items(torch, items, rank: int, world: int, shard: str) -> list:
 
     if world == 1 or shard != "paths":
         return items
-    owners = host_path_owners(world)
+    owners = host_path_owners(world, rates=rates, base_bytes=base_bytes)
     out = [SimpleNamespace(name=s.name, first_case=0,
                            d=torch.empty(CASES_PER_PATH, dtype=torch.int32, device="meta"))
            for s in workloads.validation_paths() if owners[s.name] == rank]
@@ -655,6 +655,27 @@ def run_ours(args) -> int:
     host = host_step(torch, dev, e2e_items(torch, items, rank, world, args.shard))
     h2d, d2h = copy_bytes(host)
     e2e_step(t5, host)  # once untimed: the allocator then holds the buffers the timed runs need
+    link_gbs = None
+    if world > 1 and args.shard == "paths":
+        # the ranks' host links differ (shared uplinks and sockets): one
+        # untimed run of the step on every rank at once gives each rank's
+        # rate, and the paths are dealt again by bytes over rate
+        dist.barrier()
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        e2e_step(t5, host)
+        torch.cuda.synchronize(dev)
+        rate = torch.zeros(world, dtype=torch.float64, device=dev)
+        rate[rank] = (h2d + d2h) / (time.perf_counter() - t0) / 1e9
+        dist.all_reduce(rate, op=dist.ReduceOp.SUM)
+        link_gbs = rate.tolist()
+        tile_bytes = sum(sum(x.numel() * x.element_size() for x in xs) + res.numel() * res.element_size()
+                         for _item, kind, xs, _kw, res in host if kind == "tiles")
+        del host
+        host = host_step(torch, dev, e2e_items(torch, items, rank, world, args.shard,
+                                               rates=link_gbs, base_bytes=tile_bytes))
+        h2d, d2h = copy_bytes(host)
+        e2e_step(t5, host)
     # tile words against the timed launches' directly; each path's words by
     # their checksum, compared with the timed launches' after the reduction
     e2e_bad = sum(int((res.view(-1) != item.d.cpu().view(-1)).sum())
@@ -690,6 +711,8 @@ def run_ours(args) -> int:
         dist.all_reduce(slots, op=dist.ReduceOp.SUM)
         by_rank = {"e2e_s": slots[:, 0].tolist(), "host_copy_ceiling_s": slots[:, 1].tolist(),
                    "h2d_bytes": [int(x) for x in slots[:, 2].tolist()]}
+        if link_gbs is not None:
+            by_rank["calibration_gbs"] = link_gbs
         t = torch.tensor([elapsed_ms, e2e_s, ceiling_s, nv["ms"]["nvfp4-k64"], nv["ms"]["nvfp4-sparse-k128"],
                           *launch_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -840,7 +863,8 @@ def report_line(args, world, items, names, launches, elapsed_ms, launch_ms, valu
                 "host_copy_ceiling_s": ceiling_s, "frac_of_host_copy_ceiling": ceiling_s / e2e_s,
                 "calls": "mma_dot_batch per path and mma_batch for the tiles, raw uint32 container words in pinned "
                          "host memory, pinned out, wait=False, at most four calls in flight",
-                "assignment": ("whole paths per rank by host bytes, tile shares" if world > 1 and args.shard == "paths"
+                "assignment": ("whole paths per rank by host bytes over each rank's host-link rate from one "
+                               "calibration run, tile shares" if world > 1 and args.shard == "paths"
                                else "the timed launches' cases")},
         "clocks": clocks,
     }

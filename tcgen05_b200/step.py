@@ -108,18 +108,31 @@ def path_host_bytes(spec) -> int:
     return per
 
 
-def host_path_owners(world: int) -> dict[str, int]:
+def host_path_owners(world: int, rates=None, base_bytes: float = 0.0) -> dict[str, int]:
     """``path_owners`` weighted by host bytes instead of GPU time: for a step
-    through the public API from host memory, which the host link bounds."""
+    through the public API from host memory, which the host link bounds.
+
+    ``rates`` (one positive figure per rank, bytes per second or any common
+    unit) weights the deal by each rank's host link: a path goes to the rank
+    that would finish it first, counting ``base_bytes`` the rank moves in any
+    case (its share of the tiles).  Without rates every link counts the same
+    and the deal is by bytes alone.  Every rank computes the same deal from
+    the same rates.  A path's bytes are its per-case host bytes times
+    ``CASES_PER_PATH``, the unit of ``base_bytes``."""
     from . import workloads
 
+    if rates is None:
+        rates = [1.0] * world
+    rates = [float(x) for x in rates]
+    if len(rates) != world or min(rates) <= 0:
+        raise ValueError("rates must hold one positive figure per rank")
     specs = workloads.validation_paths()
     names = [s.name for s in specs]
-    cost = {s.name: path_host_bytes(s) for s in specs}
-    load = [0] * world
+    cost = {s.name: path_host_bytes(s) * CASES_PER_PATH for s in specs}
+    load = [float(base_bytes)] * world
     owners = {}
     for n in sorted(names, key=lambda n: (-cost[n], names.index(n))):
-        r = min(range(world), key=lambda x: (load[x], x))
+        r = min(range(world), key=lambda x: ((load[x] + cost[n]) / rates[x], x))
         owners[n] = r
         load[r] += cost[n]
     return owners

@@ -230,3 +230,30 @@ def test_host_path_owners_balance_host_bytes():
         for n, r in owners.items():
             load[r] += per[n]
         assert max(load) <= sum(load) / world + max(per.values())
+
+
+def test_host_path_owners_follow_each_ranks_link_rate():
+    """Weighted by measured host-link rates, the deal gives a slower link
+    fewer bytes and keeps every rank's time (bytes over rate, its tile bytes
+    included) within one path of the balanced time; equal rates give the
+    bytes-only deal, and the deal rejects a rate list of the wrong length."""
+    from tcgen05_b200 import step, workloads
+
+    specs = workloads.validation_paths()
+    per = {s.name: step.path_host_bytes(s) * step.CASES_PER_PATH for s in specs}
+    assert step.host_path_owners(8, rates=[5.0] * 8) == step.host_path_owners(8)
+    rates = [28e9] * 4 + [36e9] * 4
+    base = 170e6
+    owners = step.host_path_owners(8, rates=rates, base_bytes=base)
+    assert set(owners) == set(per)
+    load = [base] * 8
+    for n, r in owners.items():
+        load[r] += per[n]
+    assert max(load[:4]) < min(load[4:])
+    times = [b / x for b, x in zip(load, rates)]
+    balanced = sum(load) / sum(rates)
+    assert max(times) <= balanced + max(per.values()) / min(rates)
+    with pytest.raises(ValueError, match="one positive figure per rank"):
+        step.host_path_owners(2, rates=[1.0])
+    with pytest.raises(ValueError, match="one positive figure per rank"):
+        step.host_path_owners(2, rates=[1.0, 0.0])
