@@ -53,6 +53,7 @@ METRIC = "emulated element-MACs/s (bit-exact) at 1/2/4/8 B200 vs Python model on
 UNIT = "element-MACs/s"
 NVFP4_CASES = 1 << 24
 E2E_RUNS = 3
+E2E_CALIBRATIONS = 2  # untimed runs over N GPUs that measure each rank's host-link rate
 REF_DIR = REPO / "baseline" / "_ref"
 
 from tcgen05_b200.step import (CASES_PER_PATH, MATRIX_TILES, STEP_STREAMS, TILE_K, TILE_M, TILE_N,  # noqa: E402
@@ -655,11 +656,12 @@ def run_ours(args) -> int:
     host = host_step(torch, dev, e2e_items(torch, items, rank, world, args.shard))
     h2d, d2h = copy_bytes(host)
     e2e_step(t5, host)  # once untimed: the allocator then holds the buffers the timed runs need
-    link_gbs = None
-    if world > 1 and args.shard == "paths":
-        # the ranks' host links differ (shared uplinks and sockets): one
-        # untimed run of the step on every rank at once gives each rank's
-        # rate, and the paths are dealt again by bytes over rate
+    link_gbs = []
+    for _ in range(E2E_CALIBRATIONS if world > 1 and args.shard == "paths" else 0):
+        # the ranks' host links differ (shared uplinks and sockets), and how
+        # much depends on what the others move: an untimed run of the step on
+        # every rank at once gives each rank's rate under the current deal,
+        # and the paths are dealt again by bytes over rate
         dist.barrier()
         torch.cuda.synchronize(dev)
         t0 = time.perf_counter()
@@ -668,12 +670,12 @@ def run_ours(args) -> int:
         rate = torch.zeros(world, dtype=torch.float64, device=dev)
         rate[rank] = (h2d + d2h) / (time.perf_counter() - t0) / 1e9
         dist.all_reduce(rate, op=dist.ReduceOp.SUM)
-        link_gbs = rate.tolist()
+        link_gbs.append(rate.tolist())
         tile_bytes = sum(sum(x.numel() * x.element_size() for x in xs) + res.numel() * res.element_size()
                          for _item, kind, xs, _kw, res in host if kind == "tiles")
         del host
         host = host_step(torch, dev, e2e_items(torch, items, rank, world, args.shard,
-                                               rates=link_gbs, base_bytes=tile_bytes))
+                                               rates=link_gbs[-1], base_bytes=tile_bytes))
         h2d, d2h = copy_bytes(host)
         e2e_step(t5, host)
     # tile words against the timed launches' directly; each path's words by
@@ -711,7 +713,7 @@ def run_ours(args) -> int:
         dist.all_reduce(slots, op=dist.ReduceOp.SUM)
         by_rank = {"e2e_s": slots[:, 0].tolist(), "host_copy_ceiling_s": slots[:, 1].tolist(),
                    "h2d_bytes": [int(x) for x in slots[:, 2].tolist()]}
-        if link_gbs is not None:
+        if link_gbs:
             by_rank["calibration_gbs"] = link_gbs
         t = torch.tensor([elapsed_ms, e2e_s, ceiling_s, nv["ms"]["nvfp4-k64"], nv["ms"]["nvfp4-sparse-k128"],
                           *launch_ms], dtype=torch.float64, device=dev)
@@ -863,9 +865,9 @@ def report_line(args, world, items, names, launches, elapsed_ms, launch_ms, valu
                 "host_copy_ceiling_s": ceiling_s, "frac_of_host_copy_ceiling": ceiling_s / e2e_s,
                 "calls": "mma_dot_batch per path and mma_batch for the tiles, raw uint32 container words in pinned "
                          "host memory, pinned out, wait=False, at most four calls in flight",
-                "assignment": ("whole paths per rank by host bytes over each rank's host-link rate from one "
-                               "calibration run, tile shares" if world > 1 and args.shard == "paths"
-                               else "the timed launches' cases")},
+                "assignment": (f"whole paths per rank by host bytes over each rank's host-link rate, from "
+                               f"{E2E_CALIBRATIONS} calibration runs, tile shares"
+                               if world > 1 and args.shard == "paths" else "the timed launches' cases")},
         "clocks": clocks,
     }
 
