@@ -257,3 +257,47 @@ def test_host_path_owners_follow_each_ranks_link_rate():
         step.host_path_owners(2, rates=[1.0])
     with pytest.raises(ValueError, match="one positive figure per rank"):
         step.host_path_owners(2, rates=[1.0, 0.0])
+
+
+def _deal_worker(rank, world, port, q):
+    """One rank of the end-to-end step's calibrated deal: its own host-link
+    rate goes round an all-reduce, as bench.py does it, and the rank
+    computes the deal from the reduced rates."""
+    import torch
+    import torch.distributed as dist
+
+    from tcgen05_b200 import step
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rate = torch.zeros(world, dtype=torch.float64)
+        rate[rank] = 23.2 if rank == 0 else 34.7  # GB/s, the two link classes of an 8-GPU box
+        dist.all_reduce(rate, op=dist.ReduceOp.SUM)
+        q.put((rank, step.host_path_owners(world, rates=rate.tolist(), base_bytes=170e6)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_calibrated_deal_is_the_same_on_every_rank_over_gloo():
+    """Both ranks reach the same deal from the all-reduced rates, every path
+    has one owner, and the rank with the slower link moves fewer bytes."""
+    import multiprocessing as mp
+
+    from tcgen05_b200 import step, workloads
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30000 + os.getpid() % 1000
+    procs = [ctx.Process(target=_deal_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert got[0] == got[1]
+    per = {s.name: step.path_host_bytes(s) * step.CASES_PER_PATH for s in workloads.validation_paths()}
+    assert set(got[0]) == set(per)
+    load = [sum(per[n] for n, r in got[0].items() if r == k) for k in (0, 1)]
+    assert load[0] < load[1]
